@@ -1,0 +1,187 @@
+/*
+ * qmla — B200 (sm_100a) paged latent-KV MLA / GLA decode attention.
+ *
+ * C ABI of libqmla.so.  Plain pointers and sizes only; every device pointer is
+ * a CUDA device address, `stream` is a cudaStream_t passed as void*.  No entry
+ * point allocates device memory, synchronises the device, or touches host
+ * memory other than the parameter structs, so each one may be recorded into a
+ * CUDA graph.  Entry points return 0 on success or a negative QMLA_E_* code.
+ *
+ * Reference interfaces replaced (paths inside sootaugur/qwen-mla-vllm):
+ *   qmla_mla_decode   <- qwen_mla/ops/mla_decode_attention.py:1264-1359
+ *                        decode_attention_fwd(q, k_buffer, v_buffer, o, lse,
+ *                        req_to_token, b_seq_len, attn_logits, num_kv_splits,
+ *                        sm_scale, page_size, logit_cap, k_scale, v_scale,
+ *                        is_mla, rms_offset, rms_bf16, rms_log8, qrows), and
+ *                        the FlashInfer fork's run() called from
+ *                        qwen_mla/fi_decode.py:381-384 (BatchMLAPagedAttention
+ *                        launcher, qwen_mla/kernels/qwen_mla.cuh:1386-1480).
+ *   qmla_plan         <- qwen_mla/fi_decode.py:235-270 (_RankPlan.plan_cpu) and
+ *                        the MLAPlan work partition it feeds
+ *                        (qwen_mla/kernels/qwen_scheduler.cuh:1599-1871).
+ *   qmla_dcp_correct  <- qwen_mla/dcp_fix.py:31-130 (_mla_correct_attn_out).
+ *   qmla_dcp_merge    <- the all-gather + correct + reduce-scatter sequence of
+ *                        vLLM's cp_lse_ag_out_rs that dcp_fix.py:133-142 patches,
+ *                        fused into one merge of N (out, lse) partials.
+ *   qmla_fp8_cache_write <- qwen_mla/mla_impl.py:309-342
+ *                        (QwenMLATritonImpl.do_kv_cache_update, FP8 row writer).
+ */
+#ifndef QMLA_H_
+#define QMLA_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* error codes */
+#define QMLA_OK 0
+#define QMLA_E_INVALID (-1)        /* bad argument (null pointer, negative size, ...) */
+#define QMLA_E_UNSUPPORTED (-2)    /* shape / dtype combination this build has no kernel for */
+#define QMLA_E_ALIGNMENT (-3)      /* a pointer or stride breaks the 16-byte TMA rule */
+#define QMLA_E_WORKSPACE (-4)      /* workspace smaller than qmla_decode_workspace_bytes() */
+#define QMLA_E_CUDA (-5)           /* a CUDA runtime / driver call failed */
+#define QMLA_E_DEVICE_TIMEOUT (-6) /* a kernel gave up waiting (see qmla_read_status) */
+
+/* element types */
+#define QMLA_DT_BF16 0
+#define QMLA_DT_F16 1
+#define QMLA_DT_F32 2
+#define QMLA_DT_FP8E4M3 3
+
+/* how the per-(token, head) score divisor is stored in the cache row
+ * (qwen_mla/ops/mla_decode_attention.py:466-505) */
+#define QMLA_RMS_NONE 0   /* rms_offset < 0: no divide                                  */
+#define QMLA_RMS_NATIVE 1 /* one element per head in the cache dtype (bf16; e4m3 x k_scale) */
+#define QMLA_RMS_BF16 2   /* FP8 row, raw bf16, two bytes per head                       */
+#define QMLA_RMS_LOG8 3   /* FP8 row, uint8 code of log2(rms) over [-3, 3]               */
+
+typedef struct qmla_decode_params {
+  /* Query rows.  Element (row, head, d):
+   *   d <  rank        : q   [row*q_stride_row   + head*q_stride_head   + d]
+   *   rank <= d < qk_dim: q_pe[row*qpe_stride_row + head*qpe_stride_head + d - rank]
+   * Pass q_pe = q + rank (same strides) for a single [rows, heads, Lq] tensor. */
+  const void* q;
+  int64_t q_stride_row, q_stride_head;
+  const void* q_pe;
+  int64_t qpe_stride_row, qpe_stride_head;
+  int32_t q_dtype; /* QMLA_DT_BF16 or QMLA_DT_F16 */
+
+  /* Paged latent cache: token t of page p starts at
+   * kv_cache + (p*kv_stride_page + t*kv_stride_token) elements.  One row is
+   * [latent (rank) | rope (qk_dim - rank) | rms tail | pad]. */
+  const void* kv_cache;
+  int64_t kv_stride_page, kv_stride_token;
+  int64_t kv_num_pages;
+  int32_t kv_row_width; /* elements per row that may be read */
+  int32_t kv_dtype;     /* QMLA_DT_BF16, QMLA_DT_F16 or QMLA_DT_FP8E4M3 */
+  int32_t page_size;    /* tokens per page, a multiple of 16 */
+
+  /* block_table[row*block_table_stride + i] is the i-th page of a row;
+   * seq_lens[row] its length in tokens (values < 0 are treated as 0). */
+  const int32_t* block_table;
+  int64_t block_table_stride;
+  const int32_t* seq_lens;
+
+  int32_t num_rows;   /* decode rows (already flattened for MTP verify)      */
+  int32_t num_heads;  /* query heads per row (<= 32)                          */
+  int32_t rank;       /* latent width = value width (multiple of 128)        */
+  int32_t qk_dim;     /* attention width: latent + rope (reference Lk)        */
+  int32_t rms_offset; /* element (byte for FP8 rows) offset of the rms tail  */
+  int32_t rms_mode;   /* QMLA_RMS_*                                           */
+  float sm_scale;
+  float logit_cap;      /* <= 0: off                                          */
+  const float* k_scale; /* device fp32 scalar, FP8 dequant scale; NULL = 1.0  */
+  int32_t qrows;        /* MTP verify tokens per request (rows already flattened) */
+
+  /* Outputs: o[row*o_stride_row + head*o_stride_head + d], d < rank;
+   * lse[row*lse_stride_row + head] natural-log LSE of the scaled scores
+   * (may be NULL). */
+  void* o;
+  int64_t o_stride_row, o_stride_head;
+  int32_t o_dtype; /* QMLA_DT_BF16, QMLA_DT_F16 or QMLA_DT_F32 */
+  void* lse;
+  int64_t lse_stride_row;
+  int32_t lse_dtype; /* QMLA_DT_F32, QMLA_DT_BF16 or QMLA_DT_F16 */
+
+  /* Caller-owned device scratch of at least qmla_decode_workspace_bytes(). */
+  void* workspace;
+  int64_t workspace_bytes;
+
+  /* Optional precomputed plan from qmla_plan (device copy of tile_prefix,
+   * num_rows + 1 entries).  NULL: the plan is built on the device. */
+  const int32_t* plan_tile_prefix;
+
+  int32_t num_ctas; /* persistent CTAs; 0 = one per SM */
+  int32_t device;   /* CUDA device ordinal the pointers live on */
+} qmla_decode_params;
+
+/* Bytes of workspace qmla_mla_decode needs for these parameters. */
+int qmla_decode_workspace_bytes(const qmla_decode_params* p, int64_t* bytes);
+
+/* Paged MLA decode: o, lse <- softmax((q . k) / rms * sm_scale) . v per row
+ * and head, reading each row's cache once.  Launches a plan kernel (unless
+ * plan_tile_prefix is given), the persistent decode kernel and a merge
+ * kernel on `stream`. */
+int qmla_mla_decode(const qmla_decode_params* p, void* stream);
+
+/* Device status word of the last call that used `workspace`: 0, or bit 0 set
+ * when a kernel wait timed out.  Copies 4 bytes device->host on `stream` and
+ * synchronises that stream (host-side diagnostic, not for graph capture). */
+int qmla_read_status(const void* workspace, void* stream, int32_t* status);
+
+/* Host planner (no CUDA calls).  From host sequence lengths it writes, into
+ * caller-owned host arrays:
+ *   tile_prefix[num_rows+1]  exclusive prefix of ceil(len/64) (the decode
+ *                            kernel's work partition; copy it to the device
+ *                            and pass as plan_tile_prefix),
+ *   kv_indptr[num_rows+1]    page-count prefix  (fi_decode.py:235-270),
+ *   kv_len[num_rows]         clamped lengths,
+ * and *total_tiles / *total_pages.  kv_indptr / kv_len may be NULL. */
+int qmla_plan(const int32_t* seq_lens_host, int32_t num_rows, int32_t page_size,
+              int32_t* tile_prefix, int32_t* kv_indptr, int32_t* kv_len,
+              int64_t* total_tiles, int64_t* total_pages);
+
+/* DCP output correction for one rank (dcp_fix.py:31-130):
+ *   lse_g[b,h] = logsumexp_n lses[n,b,h]  (NaN / +inf treated as -inf)
+ *   out[b,h,:] *= exp(lses[cp_rank,b,h] - lse_g[b,h])  (0 where the factor is 0)
+ * out: [B,H,D] (dtype out_dtype, strides in elements), lses: [N,B,H] fp32,
+ * lse_out: [B,H] fp32 (may be NULL). */
+int qmla_dcp_correct(void* out, int32_t out_dtype, int64_t out_stride_b, int64_t out_stride_h,
+                     const float* lses, int64_t lses_stride_n, int64_t lses_stride_b,
+                     float* lse_out, int32_t n_ranks, int32_t cp_rank, int32_t B, int32_t H,
+                     int32_t D, int32_t is_base_e, void* stream);
+
+/* Fused DCP merge of N partial results (what correct + reduce-scatter compute
+ * together): o = sum_n exp(lse_n - lse_g) * o_n, lse = lse_g.
+ * parts: [N,B,H,D] dtype parts_dtype, contiguous; part_lse: [N,B,H] fp32
+ * (natural log); o: [B,H,D] o_dtype contiguous; lse: [B,H] fp32 (may be NULL). */
+int qmla_dcp_merge(const void* parts, int32_t parts_dtype, const float* part_lse, void* o,
+                   int32_t o_dtype, float* lse, int32_t n_parts, int32_t B, int32_t H, int32_t D,
+                   void* stream);
+
+/* FP8 cache writer (mla_impl.py:309-342): for each token i with slot
+ * s = max(slot_mapping[i], 0), writes row s of the byte cache as
+ *   [e4m3(latent/k_scale) | e4m3(rope/k_scale) | rms tail | untouched pad]
+ * with values clamped to +-448 and rounded to nearest-even; the rms tail is
+ * one log8 code per head (rms_mode QMLA_RMS_LOG8) or two bf16 bytes per head
+ * (QMLA_RMS_BF16).  latent: [n, rank] bf16, k_pe: [n, >= rope + heads] bf16
+ * ([rope | rms | ...]), row strides in elements; cache rows are
+ * cache_row_stride bytes apart (slot = page*page_size + token). */
+int qmla_fp8_cache_write(const void* latent, int64_t latent_stride, const void* k_pe,
+                         int64_t k_pe_stride, const int64_t* slot_mapping, int32_t n_tokens,
+                         int32_t rank, int32_t rope, int32_t heads, int32_t rms_mode,
+                         const float* k_scale, void* cache, int64_t cache_row_stride,
+                         void* stream);
+
+/* Human-readable text for a QMLA_E_* code. */
+const char* qmla_error_string(int code);
+
+/* ABI version (major*100 + minor). */
+int qmla_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QMLA_H_ */

@@ -1,0 +1,462 @@
+// libqmla: C-ABI entry points (include/qmla.h) over the sm_100a kernels.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "qmla.h"
+#include "qmla_aux.cuh"
+#include "qmla_decode.cuh"
+
+using namespace qmla;
+
+namespace {
+
+constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in limit per block on sm_100
+
+struct DevInfo {
+  int sms = 0;
+  int max_smem = 0;
+  bool ok = false;
+};
+
+std::mutex g_mu;
+std::map<int, DevInfo> g_dev;
+
+DevInfo dev_info(int dev) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_dev.find(dev);
+  if (it != g_dev.end()) return it->second;
+  DevInfo d;
+  if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+      cudaDeviceGetAttribute(&d.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) ==
+          cudaSuccess)
+    d.ok = true;
+  g_dev[dev] = d;
+  return d;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+using MapKey = std::tuple<const void*, int, int, int, int64_t, int64_t, int64_t, int, int>;
+std::map<MapKey, CUtensorMap> g_maps;
+
+// 3-D map over the paged cache: (row element, token in page, page).  Each
+// box is one 128-byte column of `run` consecutive tokens of one page.
+int cache_tensor_map(const qmla_decode_params* p, int run, CUtensorMap* out) {
+  const bool fp8 = p->kv_dtype == QMLA_DT_FP8E4M3;
+  const int es = fp8 ? 1 : 2;
+  MapKey key{p->kv_cache, p->kv_dtype, p->kv_row_width, p->page_size, p->kv_num_pages,
+             p->kv_stride_page, p->kv_stride_token, run, 0};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+      *out = it->second;
+      return QMLA_OK;
+    }
+  }
+  auto fn = encode_fn();
+  if (!fn) return QMLA_E_CUDA;
+  CUtensorMapDataType dt = fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                               : (p->kv_dtype == QMLA_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+  cuuint64_t dims[3] = {(cuuint64_t)p->kv_row_width, (cuuint64_t)p->page_size,
+                        (cuuint64_t)p->kv_num_pages};
+  cuuint64_t strides[2] = {(cuuint64_t)(p->kv_stride_token * es),
+                           (cuuint64_t)(p->kv_stride_page * es)};
+  cuuint32_t box[3] = {(cuuint32_t)(128 / es), (cuuint32_t)run, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUtensorMap m;
+  CUresult r = fn(&m, dt, 3, const_cast<void*>(p->kv_cache), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return QMLA_E_ALIGNMENT;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_maps.size() > 4096) g_maps.clear();
+  g_maps[key] = m;
+  *out = m;
+  return QMLA_OK;
+}
+
+int gcd_int(int a, int b) {
+  while (b) {
+    int t = a % b;
+    a = b;
+    b = t;
+  }
+  return a;
+}
+
+int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+struct Plan {
+  int npv, nb, nqk;
+  int n_sub_qk, n_slot_tile, n_land_tile;
+  int run;
+  int G;
+  int rms_bytes;
+  // workspace offsets
+  int64_t ws_status, ws_prefix, ws_plse, ws_po, ws_total;
+  // smem
+  uint32_t off_ring, nslot, off_q, q_chunk, off_p, p_bytes, off_land, nland, off_rms, off_misc;
+  uint32_t smem_total;
+};
+
+int make_plan(const qmla_decode_params* p, Plan* pl) {
+  if (!p || !p->q || !p->kv_cache || !p->block_table || !p->seq_lens || !p->o)
+    return QMLA_E_INVALID;
+  if (!p->q_pe && p->qk_dim > p->rank) return QMLA_E_INVALID;
+  if (p->num_rows < 0 || p->num_heads <= 0 || p->num_heads > 32) return QMLA_E_UNSUPPORTED;
+  if (p->rank <= 0 || p->rank % 128 != 0) return QMLA_E_UNSUPPORTED;
+  const int nb = p->rank / 128;
+  if (!(nb == 2 || nb == 3 || nb == 4 || nb == 6)) return QMLA_E_UNSUPPORTED;
+  if (p->qk_dim < p->rank || p->qk_dim > 1024) return QMLA_E_UNSUPPORTED;
+  if (p->page_size <= 0 || p->page_size % 16 != 0) return QMLA_E_UNSUPPORTED;
+  if (p->q_dtype != QMLA_DT_BF16 && p->q_dtype != QMLA_DT_F16) return QMLA_E_UNSUPPORTED;
+  if (p->o_dtype < 0 || p->o_dtype > 2) return QMLA_E_UNSUPPORTED;
+  if (p->lse && (p->lse_dtype < 0 || p->lse_dtype > 2)) return QMLA_E_UNSUPPORTED;
+  const bool fp8 = p->kv_dtype == QMLA_DT_FP8E4M3;
+  if (!fp8 && p->kv_dtype != QMLA_DT_BF16) return QMLA_E_UNSUPPORTED;  // f16 caches: not built
+  if (p->rms_mode < 0 || p->rms_mode > 3) return QMLA_E_INVALID;
+  if (!fp8 && p->rms_mode >= 2) return QMLA_E_INVALID;
+  const int es = fp8 ? 1 : 2;
+  if (reinterpret_cast<uintptr_t>(p->kv_cache) % 16 != 0) return QMLA_E_ALIGNMENT;
+  if ((p->kv_stride_token * es) % 16 != 0 || (p->kv_stride_page * es) % 16 != 0)
+    return QMLA_E_ALIGNMENT;
+  if (p->kv_row_width < p->qk_dim) return QMLA_E_INVALID;
+
+  pl->nb = nb;
+  pl->npv = p->num_heads <= 16 ? 16 : 32;
+  pl->nqk = (p->num_heads + 7) / 8 * 8;
+  pl->run = gcd_int(p->page_size, kTile);
+  pl->rms_bytes = p->rms_mode == QMLA_RMS_NONE ? 0
+                  : p->rms_mode == QMLA_RMS_BF16 ? 2 * p->num_heads
+                                                 : p->num_heads;
+  int rms_end = p->rms_mode == QMLA_RMS_NONE ? 0 : p->rms_offset + pl->rms_bytes;
+  if (p->rms_mode != QMLA_RMS_NONE && (p->rms_offset < p->qk_dim || rms_end > p->kv_row_width))
+    return QMLA_E_INVALID;
+  if (!fp8) {
+    int need = std::max(p->qk_dim, rms_end);
+    pl->n_sub_qk = (need + 63) / 64;
+    pl->n_slot_tile = (pl->n_sub_qk + 1) / 2;
+    pl->n_land_tile = 0;
+  } else {
+    pl->n_sub_qk = (p->qk_dim + 63) / 64;
+    pl->n_slot_tile = (p->qk_dim + 127) / 128;
+    pl->n_land_tile = (std::max(p->qk_dim, rms_end) + 127) / 128;
+    if (2 * p->num_heads > 64) return QMLA_E_UNSUPPORTED;
+  }
+  if (pl->n_sub_qk > kMaxQkChunks) return QMLA_E_UNSUPPORTED;
+  if (pl->n_slot_tile < nb) return QMLA_E_INVALID;
+
+  DevInfo di = dev_info(p->device);
+  if (!di.ok) return QMLA_E_CUDA;
+  int G = p->num_ctas > 0 ? p->num_ctas : di.sms;
+  G = std::min(G, kMaxCtas);
+  pl->G = G;
+
+  // shared memory map
+  uint32_t off = 0;
+  pl->q_chunk = (uint32_t)((pl->nqk + 7) / 8 * 1024);
+  uint32_t q_bytes = pl->q_chunk * pl->n_sub_qk;
+  pl->p_bytes = (uint32_t)(pl->npv * 128);
+  uint32_t misc_bytes = 2048;
+  uint32_t rms_bytes_smem = fp8 ? 2 * kTile * 64 : 0;
+  uint32_t fixed = q_bytes + 2 * pl->p_bytes + misc_bytes + rms_bytes_smem + 1024 /*align slack*/;
+  int budget = std::min(di.max_smem, kMaxDynSmem) - (int)fixed;
+  if (!fp8) {
+    int ns = budget / kSlotBytes;
+    if (ns < pl->n_slot_tile) return QMLA_E_UNSUPPORTED;
+    pl->nslot = (uint32_t)std::min(ns, 3 * pl->n_slot_tile);
+    pl->nland = 0;
+  } else {
+    pl->nslot = (uint32_t)pl->n_slot_tile;
+    int nl = (budget - (int)pl->nslot * kSlotBytes) / kLandBytes;
+    if (nl < 2) return QMLA_E_UNSUPPORTED;
+    pl->nland = (uint32_t)std::min(nl, 3 * pl->n_land_tile);
+  }
+  pl->off_ring = off;
+  off += pl->nslot * kSlotBytes;
+  pl->off_land = off;
+  off += pl->nland * kLandBytes;
+  pl->off_q = off;
+  off += q_bytes;
+  pl->off_p = off;
+  off += 2 * pl->p_bytes;
+  pl->off_rms = off;
+  off += rms_bytes_smem;
+  pl->off_misc = (uint32_t)align_up(off, 16);
+  off = pl->off_misc + misc_bytes;
+  pl->smem_total = off + 1024;
+
+  // workspace map
+  int64_t w = 0;
+  pl->ws_status = w;
+  w += 256;
+  pl->ws_prefix = w;
+  w = align_up(w + 4 * ((int64_t)p->num_rows + 1), 256);
+  pl->ws_plse = w;
+  w = align_up(w + 4 * (int64_t)2 * G * p->num_heads, 256);
+  pl->ws_po = w;
+  w = align_up(w + 4 * (int64_t)2 * G * p->num_heads * p->rank, 256);
+  pl->ws_total = w;
+  return QMLA_OK;
+}
+
+template <bool FP8, int NB, int NPV>
+int launch_decode_t(const CUtensorMap& tmap, const DecodeArgs& a, uint32_t smem,
+                    cudaStream_t st) {
+  auto k = mla_decode_kernel<FP8, NB, NPV>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+  });
+  if (attr_err != cudaSuccess) return QMLA_E_CUDA;
+  k<<<a.G, FP8 ? 320 : 192, smem, st>>>(tmap, a);
+  return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
+}
+
+int launch_decode(bool fp8, int nb, int npv, const CUtensorMap& tmap, const DecodeArgs& a,
+                  uint32_t smem, cudaStream_t st) {
+#define QMLA_CASE(F, B, N) \
+  if (fp8 == F && nb == B && npv == N) return launch_decode_t<F, B, N>(tmap, a, smem, st);
+  QMLA_CASE(false, 6, 32)
+  QMLA_CASE(false, 6, 16)
+  QMLA_CASE(false, 3, 16)
+  QMLA_CASE(false, 3, 32)
+  QMLA_CASE(false, 2, 32)
+  QMLA_CASE(false, 2, 16)
+  QMLA_CASE(false, 4, 32)
+  QMLA_CASE(false, 4, 16)
+  QMLA_CASE(true, 6, 32)
+  QMLA_CASE(true, 6, 16)
+  QMLA_CASE(true, 3, 16)
+  QMLA_CASE(true, 3, 32)
+  QMLA_CASE(true, 2, 32)
+  QMLA_CASE(true, 2, 16)
+  QMLA_CASE(true, 4, 32)
+  QMLA_CASE(true, 4, 16)
+#undef QMLA_CASE
+  return QMLA_E_UNSUPPORTED;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qmla_abi_version(void) { return 100; }
+
+const char* qmla_error_string(int code) {
+  switch (code) {
+    case QMLA_OK:
+      return "ok";
+    case QMLA_E_INVALID:
+      return "invalid argument";
+    case QMLA_E_UNSUPPORTED:
+      return "unsupported shape or dtype";
+    case QMLA_E_ALIGNMENT:
+      return "pointer or stride not 16-byte aligned for TMA";
+    case QMLA_E_WORKSPACE:
+      return "workspace too small";
+    case QMLA_E_CUDA:
+      return "CUDA call failed";
+    case QMLA_E_DEVICE_TIMEOUT:
+      return "device wait timed out";
+    default:
+      return "unknown error";
+  }
+}
+
+int qmla_decode_workspace_bytes(const qmla_decode_params* p, int64_t* bytes) {
+  if (!bytes) return QMLA_E_INVALID;
+  Plan pl;
+  int rc = make_plan(p, &pl);
+  if (rc != QMLA_OK) return rc;
+  *bytes = pl.ws_total;
+  return QMLA_OK;
+}
+
+int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
+  Plan pl;
+  int rc = make_plan(p, &pl);
+  if (rc != QMLA_OK) return rc;
+  if (!p->workspace || p->workspace_bytes < pl.ws_total) return QMLA_E_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(p->workspace) % 256 != 0) return QMLA_E_ALIGNMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess) return QMLA_E_CUDA;
+  if (cur != p->device && cudaSetDevice(p->device) != cudaSuccess) return QMLA_E_CUDA;
+
+  uint8_t* ws = reinterpret_cast<uint8_t*>(p->workspace);
+  DecodeArgs a;
+  memset(&a, 0, sizeof(a));
+  a.q = reinterpret_cast<const uint8_t*>(p->q);
+  a.q_pe = reinterpret_cast<const uint8_t*>(p->q_pe ? p->q_pe : p->q);
+  a.q_sr = p->q_stride_row;
+  a.q_sh = p->q_stride_head;
+  a.qpe_sr = p->q_pe ? p->qpe_stride_row : p->q_stride_row;
+  a.qpe_sh = p->q_pe ? p->qpe_stride_head : p->q_stride_head;
+  a.q_dtype = p->q_dtype;
+  a.block_table = p->block_table;
+  a.bt_stride = p->block_table_stride;
+  a.seq_lens = p->seq_lens;
+  a.kv_num_pages = p->kv_num_pages;
+  a.page_size = p->page_size;
+  a.run_rows = pl.run;
+  a.num_rows = p->num_rows;
+  a.H = p->num_heads;
+  a.rank = p->rank;
+  a.qk_dim = p->qk_dim;
+  a.rms_offset = p->rms_offset;
+  a.rms_mode = p->rms_mode;
+  a.nqk = pl.nqk;
+  a.n_sub_qk = pl.n_sub_qk;
+  a.n_slot_tile = pl.n_slot_tile;
+  a.n_land_tile = pl.n_land_tile;
+  a.rms_slot = 0;
+  a.score_scale = p->sm_scale;
+  a.logit_cap = p->logit_cap;
+  a.k_scale = p->k_scale;
+  a.o = reinterpret_cast<uint8_t*>(p->o);
+  a.o_sr = p->o_stride_row;
+  a.o_sh = p->o_stride_head;
+  a.o_dtype = p->o_dtype;
+  a.lse = reinterpret_cast<uint8_t*>(p->lse);
+  a.lse_sr = p->lse_stride_row;
+  a.lse_dtype = p->lse_dtype;
+  a.status = reinterpret_cast<int*>(ws + pl.ws_status);
+  a.tile_prefix = p->plan_tile_prefix ? p->plan_tile_prefix
+                                      : reinterpret_cast<const int32_t*>(ws + pl.ws_prefix);
+  a.part_lse = reinterpret_cast<float*>(ws + pl.ws_plse);
+  a.part_o = reinterpret_cast<float*>(ws + pl.ws_po);
+  a.G = pl.G;
+  a.off_ring = pl.off_ring;
+  a.nslot = pl.nslot;
+  a.off_q = pl.off_q;
+  a.q_chunk_bytes = pl.q_chunk;
+  a.off_p = pl.off_p;
+  a.p_bytes = pl.p_bytes;
+  a.off_land = pl.off_land;
+  a.nland = pl.nland;
+  a.off_rms = pl.off_rms;
+  a.off_misc = pl.off_misc;
+
+  if (p->num_rows == 0) return QMLA_OK;
+  CUtensorMap tmap;
+  rc = cache_tensor_map(p, pl.run, &tmap);
+  if (rc != QMLA_OK) return rc;
+
+  if (!p->plan_tile_prefix) {
+    plan_kernel<<<1, 1024, 0, st>>>(p->seq_lens, p->num_rows,
+                                    reinterpret_cast<int32_t*>(ws + pl.ws_prefix), a.status);
+  } else {
+    if (cudaMemsetAsync(a.status, 0, 4, st) != cudaSuccess) return QMLA_E_CUDA;
+  }
+  if (cudaGetLastError() != cudaSuccess) return QMLA_E_CUDA;
+  rc = launch_decode(p->kv_dtype == QMLA_DT_FP8E4M3, pl.nb, pl.npv, tmap, a, pl.smem_total, st);
+  if (rc != QMLA_OK) return rc;
+  split_merge_kernel<<<p->num_rows, 256, 0, st>>>(a);
+  return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
+}
+
+int qmla_read_status(const void* workspace, void* stream, int32_t* status) {
+  if (!workspace || !status) return QMLA_E_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(status, workspace, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return QMLA_E_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return QMLA_E_CUDA;
+  return QMLA_OK;
+}
+
+int qmla_plan(const int32_t* seq_lens_host, int32_t num_rows, int32_t page_size,
+              int32_t* tile_prefix, int32_t* kv_indptr, int32_t* kv_len, int64_t* total_tiles,
+              int64_t* total_pages) {
+  if (!seq_lens_host || !tile_prefix || num_rows < 0 || page_size <= 0) return QMLA_E_INVALID;
+  int64_t t = 0, pg = 0;
+  tile_prefix[0] = 0;
+  if (kv_indptr) kv_indptr[0] = 0;
+  for (int i = 0; i < num_rows; ++i) {
+    int L = seq_lens_host[i] > 0 ? seq_lens_host[i] : 0;
+    t += (L + kTile - 1) / kTile;
+    pg += (L + page_size - 1) / page_size;
+    if (t > INT32_MAX || pg > INT32_MAX) return QMLA_E_UNSUPPORTED;
+    tile_prefix[i + 1] = (int32_t)t;
+    if (kv_indptr) kv_indptr[i + 1] = (int32_t)pg;
+    if (kv_len) kv_len[i] = L;
+  }
+  if (total_tiles) *total_tiles = t;
+  if (total_pages) *total_pages = pg;
+  return QMLA_OK;
+}
+
+int qmla_dcp_correct(void* out, int32_t out_dtype, int64_t out_stride_b, int64_t out_stride_h,
+                     const float* lses, int64_t lses_stride_n, int64_t lses_stride_b,
+                     float* lse_out, int32_t n_ranks, int32_t cp_rank, int32_t B, int32_t H,
+                     int32_t D, int32_t is_base_e, void* stream) {
+  if (!out || !lses || n_ranks <= 0 || cp_rank < 0 || cp_rank >= n_ranks || B < 0 || H <= 0 ||
+      D <= 0 || out_dtype < 0 || out_dtype > 2)
+    return QMLA_E_INVALID;
+  if (B == 0) return QMLA_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  dcp_correct_kernel<<<dim3(B, H), 128, 0, st>>>(reinterpret_cast<uint8_t*>(out), out_dtype,
+                                                 out_stride_b, out_stride_h, lses, lses_stride_n,
+                                                 lses_stride_b, lse_out, n_ranks, cp_rank, H, D,
+                                                 is_base_e);
+  return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
+}
+
+int qmla_dcp_merge(const void* parts, int32_t parts_dtype, const float* part_lse, void* o,
+                   int32_t o_dtype, float* lse, int32_t n_parts, int32_t B, int32_t H, int32_t D,
+                   void* stream) {
+  if (!parts || !part_lse || !o || n_parts <= 0 || n_parts > 64 || B < 0 || H <= 0 || D <= 0 ||
+      parts_dtype < 0 || parts_dtype > 2 || o_dtype < 0 || o_dtype > 2)
+    return QMLA_E_INVALID;
+  if (B == 0) return QMLA_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  dcp_merge_kernel<<<dim3(B, H), 128, 0, st>>>(reinterpret_cast<const uint8_t*>(parts),
+                                               parts_dtype, part_lse,
+                                               reinterpret_cast<uint8_t*>(o), o_dtype, lse,
+                                               n_parts, B, H, D);
+  return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
+}
+
+int qmla_fp8_cache_write(const void* latent, int64_t latent_stride, const void* k_pe,
+                         int64_t k_pe_stride, const int64_t* slot_mapping, int32_t n_tokens,
+                         int32_t rank, int32_t rope, int32_t heads, int32_t rms_mode,
+                         const float* k_scale, void* cache, int64_t cache_row_stride,
+                         void* stream) {
+  if (!latent || !k_pe || !slot_mapping || !cache || n_tokens < 0 || rank <= 0 || rope < 0 ||
+      heads <= 0 || (rms_mode != QMLA_RMS_LOG8 && rms_mode != QMLA_RMS_BF16))
+    return QMLA_E_INVALID;
+  int rb = rms_mode == QMLA_RMS_LOG8 ? heads : 2 * heads;
+  if (cache_row_stride < rank + rope + rb) return QMLA_E_INVALID;
+  if (n_tokens == 0) return QMLA_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  fp8_cache_write_kernel<<<n_tokens, 256, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(latent), latent_stride,
+      reinterpret_cast<const __nv_bfloat16*>(k_pe), k_pe_stride, slot_mapping, rank, rope, heads,
+      rms_mode, k_scale, reinterpret_cast<uint8_t*>(cache), cache_row_stride);
+  return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
+}
+
+}  // extern "C"
