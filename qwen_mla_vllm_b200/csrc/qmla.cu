@@ -110,14 +110,15 @@ int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
 struct Plan {
   int npv, nb, nqk;
-  int n_sub_qk, n_slot_tile, n_land_tile;
+  int n_slot_tile, n_qk_slots, n_sub_qk, fix_slot0;
   int run;
   int G;
   int rms_bytes;
+  int q_vec, qpe_vec;
   // workspace offsets
   int64_t ws_status, ws_prefix, ws_plse, ws_po, ws_total;
   // smem
-  uint32_t off_ring, nslot, off_q, q_chunk, off_p, p_bytes, off_land, nland, off_rms, off_misc;
+  uint32_t off_ring, nslot, off_q, q_chunk, off_p, p_bytes, off_rms, off_misc;
   uint32_t smem_total;
 };
 
@@ -145,28 +146,38 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   if (p->kv_row_width < p->qk_dim) return QMLA_E_INVALID;
 
   pl->nb = nb;
-  pl->npv = p->num_heads <= 16 ? 16 : 32;
-  pl->nqk = (p->num_heads + 7) / 8 * 8;
+  pl->nqk = p->num_heads <= 16 ? 16 : p->num_heads <= 24 ? 24 : 32;
+  pl->npv = pl->nqk <= 16 ? 16 : 32;
   pl->run = gcd_int(p->page_size, kTile);
   pl->rms_bytes = p->rms_mode == QMLA_RMS_NONE ? 0
                   : p->rms_mode == QMLA_RMS_BF16 ? 2 * p->num_heads
                                                  : p->num_heads;
-  int rms_end = p->rms_mode == QMLA_RMS_NONE ? 0 : p->rms_offset + pl->rms_bytes;
+  const int rms_end = p->rms_mode == QMLA_RMS_NONE ? 0 : p->rms_offset + pl->rms_bytes;
   if (p->rms_mode != QMLA_RMS_NONE && (p->rms_offset < p->qk_dim || rms_end > p->kv_row_width))
     return QMLA_E_INVALID;
-  if (!fp8) {
-    int need = std::max(p->qk_dim, rms_end);
-    pl->n_sub_qk = (need + 63) / 64;
-    pl->n_slot_tile = (pl->n_sub_qk + 1) / 2;
-    pl->n_land_tile = 0;
-  } else {
-    pl->n_sub_qk = (p->qk_dim + 63) / 64;
-    pl->n_slot_tile = (p->qk_dim + 127) / 128;
-    pl->n_land_tile = (std::max(p->qk_dim, rms_end) + 127) / 128;
-    if (2 * p->num_heads > 64) return QMLA_E_UNSUPPORTED;
+  // slots are 128 dims (elements of a bf16 row, bytes of an FP8 row)
+  pl->n_slot_tile = (std::max(p->qk_dim, rms_end) + 127) / 128;
+  pl->n_qk_slots = (p->qk_dim + 127) / 128;
+  pl->n_sub_qk = fp8 ? pl->n_qk_slots : (p->qk_dim + 63) / 64;
+  pl->fix_slot0 = -1;
+  if (fp8) {
+    int lo = 1 << 30;
+    if (p->qk_dim % 128 != 0) lo = p->qk_dim;
+    if (p->rms_mode != QMLA_RMS_NONE) lo = std::min(lo, p->rms_offset);
+    if (lo < (1 << 30)) pl->fix_slot0 = lo / 128;
+    if (pl->rms_bytes > 64) return QMLA_E_UNSUPPORTED;
   }
   if (pl->n_sub_qk > kMaxQkChunks) return QMLA_E_UNSUPPORTED;
-  if (pl->n_slot_tile < nb) return QMLA_E_INVALID;
+  if (pl->n_qk_slots < nb) return QMLA_E_INVALID;
+  // 16-byte vector loads of q rows (bf16 only; element strides in 2-byte units)
+  auto vec_ok = [](const void* ptr, int64_t sr, int64_t sh) {
+    return reinterpret_cast<uintptr_t>(ptr) % 16 == 0 && (sr * 2) % 16 == 0 && (sh * 2) % 16 == 0;
+  };
+  pl->q_vec = p->q_dtype == QMLA_DT_BF16 && vec_ok(p->q, p->q_stride_row, p->q_stride_head);
+  const void* qpe = p->q_pe ? p->q_pe : p->q;
+  int64_t psr = p->q_pe ? p->qpe_stride_row : p->q_stride_row;
+  int64_t psh = p->q_pe ? p->qpe_stride_head : p->q_stride_head;
+  pl->qpe_vec = p->q_dtype == QMLA_DT_BF16 && vec_ok(qpe, psr, psh);
 
   DevInfo di = dev_info(p->device);
   if (!di.ok) return QMLA_E_CUDA;
@@ -175,35 +186,28 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   pl->G = G;
 
   // shared memory map
-  uint32_t off = 0;
-  pl->q_chunk = (uint32_t)((pl->nqk + 7) / 8 * 1024);
-  uint32_t q_bytes = pl->q_chunk * pl->n_sub_qk;
+  const uint32_t slot_bytes = fp8 ? 8192u : 16384u;
+  const int q_rows = fp8 ? 2 * pl->nqk : pl->nqk;
+  pl->q_chunk = (uint32_t)((q_rows + 7) / 8 * 1024);
+  const uint32_t q_bytes = pl->q_chunk * pl->n_sub_qk;
   pl->p_bytes = (uint32_t)(pl->npv * 128);
-  uint32_t misc_bytes = 2048;
-  uint32_t rms_bytes_smem = fp8 ? 2 * kTile * 64 : 0;
-  uint32_t fixed = q_bytes + 2 * pl->p_bytes + misc_bytes + rms_bytes_smem + 1024 /*align slack*/;
-  int budget = std::min(di.max_smem, kMaxDynSmem) - (int)fixed;
-  if (!fp8) {
-    int ns = budget / kSlotBytes;
-    if (ns < pl->n_slot_tile) return QMLA_E_UNSUPPORTED;
-    pl->nslot = (uint32_t)std::min(ns, 3 * pl->n_slot_tile);
-    pl->nland = 0;
-  } else {
-    pl->nslot = (uint32_t)pl->n_slot_tile;
-    int nl = (budget - (int)pl->nslot * kSlotBytes) / kLandBytes;
-    if (nl < 2) return QMLA_E_UNSUPPORTED;
-    pl->nland = (uint32_t)std::min(nl, 3 * pl->n_land_tile);
-  }
+  const uint32_t misc_bytes = 3072;
+  const uint32_t rms_smem = fp8 ? 2 * kTile * 64 : 0;
+  const uint32_t fixed = q_bytes + 2 * pl->p_bytes + misc_bytes + rms_smem + 1024 /*align slack*/;
+  const int budget = std::min(di.max_smem, kMaxDynSmem) - (int)fixed;
+  const int ns = budget / (int)slot_bytes;
+  if (ns < pl->n_slot_tile) return QMLA_E_UNSUPPORTED;
+  pl->nslot = (uint32_t)std::min(ns, 3 * pl->n_slot_tile);
+  if ((2 * pl->nslot + 21) * 8 + 16 + 1536 > misc_bytes) return QMLA_E_UNSUPPORTED;
+  uint32_t off = 0;
   pl->off_ring = off;
-  off += pl->nslot * kSlotBytes;
-  pl->off_land = off;
-  off += pl->nland * kLandBytes;
+  off += pl->nslot * slot_bytes;
   pl->off_q = off;
   off += q_bytes;
   pl->off_p = off;
   off += 2 * pl->p_bytes;
   pl->off_rms = off;
-  off += rms_bytes_smem;
+  off += rms_smem;
   pl->off_misc = (uint32_t)align_up(off, 16);
   off = pl->off_misc + misc_bytes;
   pl->smem_total = off + 1024;
@@ -222,47 +226,68 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   return QMLA_OK;
 }
 
-template <bool FP8, int NB, int NPV>
+template <bool FP8, int NB, int NQK>
 int launch_decode_t(const CUtensorMap& tmap, const DecodeArgs& a, uint32_t smem,
                     cudaStream_t st) {
-  auto k = mla_decode_kernel<FP8, NB, NPV>;
+  auto k = mla_decode_kernel<FP8, NB, NQK>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
     attr_err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
   });
   if (attr_err != cudaSuccess) return QMLA_E_CUDA;
-  k<<<a.G, FP8 ? 320 : 192, smem, st>>>(tmap, a);
+  k<<<a.G, FP8 ? 384 : 352, smem, st>>>(tmap, a);
   return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
 }
 
-int launch_decode(bool fp8, int nb, int npv, const CUtensorMap& tmap, const DecodeArgs& a,
-                  uint32_t smem, cudaStream_t st) {
-#define QMLA_CASE(F, B, N) \
-  if (fp8 == F && nb == B && npv == N) return launch_decode_t<F, B, N>(tmap, a, smem, st);
-  QMLA_CASE(false, 6, 32)
-  QMLA_CASE(false, 6, 16)
-  QMLA_CASE(false, 3, 16)
-  QMLA_CASE(false, 3, 32)
-  QMLA_CASE(false, 2, 32)
-  QMLA_CASE(false, 2, 16)
-  QMLA_CASE(false, 4, 32)
-  QMLA_CASE(false, 4, 16)
-  QMLA_CASE(true, 6, 32)
-  QMLA_CASE(true, 6, 16)
-  QMLA_CASE(true, 3, 16)
-  QMLA_CASE(true, 3, 32)
-  QMLA_CASE(true, 2, 32)
-  QMLA_CASE(true, 2, 16)
-  QMLA_CASE(true, 4, 32)
-  QMLA_CASE(true, 4, 16)
-#undef QMLA_CASE
+template <bool FP8, int NB>
+int launch_decode_nb(int nqk, const CUtensorMap& tmap, const DecodeArgs& a, uint32_t smem,
+                     cudaStream_t st) {
+  switch (nqk) {
+    case 16:
+      return launch_decode_t<FP8, NB, 16>(tmap, a, smem, st);
+    case 24:
+      return launch_decode_t<FP8, NB, 24>(tmap, a, smem, st);
+    case 32:
+      return launch_decode_t<FP8, NB, 32>(tmap, a, smem, st);
+  }
   return QMLA_E_UNSUPPORTED;
 }
+
+template <bool FP8>
+int launch_decode_fp(int nb, int nqk, const CUtensorMap& tmap, const DecodeArgs& a,
+                     uint32_t smem, cudaStream_t st) {
+  switch (nb) {
+    case 2:
+      return launch_decode_nb<FP8, 2>(nqk, tmap, a, smem, st);
+    case 3:
+      return launch_decode_nb<FP8, 3>(nqk, tmap, a, smem, st);
+    case 4:
+      return launch_decode_nb<FP8, 4>(nqk, tmap, a, smem, st);
+    case 6:
+      return launch_decode_nb<FP8, 6>(nqk, tmap, a, smem, st);
+  }
+  return QMLA_E_UNSUPPORTED;
+}
+
+int launch_decode(bool fp8, int nb, int nqk, const CUtensorMap& tmap, const DecodeArgs& a,
+                  uint32_t smem, cudaStream_t st) {
+  return fp8 ? launch_decode_fp<true>(nb, nqk, tmap, a, smem, st)
+             : launch_decode_fp<false>(nb, nqk, tmap, a, smem, st);
+}
+
+#ifdef QMLA_TRACE
+unsigned long long* g_trace = nullptr;
+#endif
 
 }  // namespace
 
 extern "C" {
+
+#ifdef QMLA_TRACE
+// Diagnostic builds only: stage timestamps of CTA 0 go to this device buffer.
+void qmla_set_trace(void* dev_ptr) { g_trace = reinterpret_cast<unsigned long long*>(dev_ptr); }
+#endif
 
 int qmla_abi_version(void) { return 100; }
 
@@ -317,10 +342,11 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
   a.qpe_sr = p->q_pe ? p->qpe_stride_row : p->q_stride_row;
   a.qpe_sh = p->q_pe ? p->qpe_stride_head : p->q_stride_head;
   a.q_dtype = p->q_dtype;
+  a.q_vec = pl.q_vec;
+  a.qpe_vec = pl.qpe_vec;
   a.block_table = p->block_table;
   a.bt_stride = p->block_table_stride;
   a.seq_lens = p->seq_lens;
-  a.kv_num_pages = p->kv_num_pages;
   a.page_size = p->page_size;
   a.run_rows = pl.run;
   a.num_rows = p->num_rows;
@@ -329,12 +355,13 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
   a.qk_dim = p->qk_dim;
   a.rms_offset = p->rms_offset;
   a.rms_mode = p->rms_mode;
+  a.rms_bytes = pl.rms_bytes;
   a.nqk = pl.nqk;
-  a.n_sub_qk = pl.n_sub_qk;
   a.n_slot_tile = pl.n_slot_tile;
-  a.n_land_tile = pl.n_land_tile;
-  a.rms_slot = 0;
-  a.score_scale = p->sm_scale;
+  a.n_qk_slots = pl.n_qk_slots;
+  a.n_sub_qk = pl.n_sub_qk;
+  a.fix_slot0 = pl.fix_slot0;
+  a.sm_scale = p->sm_scale;
   a.logit_cap = p->logit_cap;
   a.k_scale = p->k_scale;
   a.o = reinterpret_cast<uint8_t*>(p->o);
@@ -356,10 +383,13 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
   a.q_chunk_bytes = pl.q_chunk;
   a.off_p = pl.off_p;
   a.p_bytes = pl.p_bytes;
-  a.off_land = pl.off_land;
-  a.nland = pl.nland;
   a.off_rms = pl.off_rms;
   a.off_misc = pl.off_misc;
+#ifdef QMLA_TRACE
+  a.trace = g_trace;
+#else
+  a.trace = nullptr;
+#endif
 
   if (p->num_rows == 0) return QMLA_OK;
   CUtensorMap tmap;
@@ -373,7 +403,7 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
     if (cudaMemsetAsync(a.status, 0, 4, st) != cudaSuccess) return QMLA_E_CUDA;
   }
   if (cudaGetLastError() != cudaSuccess) return QMLA_E_CUDA;
-  rc = launch_decode(p->kv_dtype == QMLA_DT_FP8E4M3, pl.nb, pl.npv, tmap, a, pl.smem_total, st);
+  rc = launch_decode(p->kv_dtype == QMLA_DT_FP8E4M3, pl.nb, pl.nqk, tmap, a, pl.smem_total, st);
   if (rc != QMLA_OK) return rc;
   split_merge_kernel<<<p->num_rows, 256, 0, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;

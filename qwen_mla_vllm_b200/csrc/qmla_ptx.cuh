@@ -44,6 +44,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Same, but lets the hardware suspend the thread for up to `hint_ns` while the
+// phase is incomplete (it resumes as soon as the phase completes), so waiting
+// warps do not take issue slots from working ones.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 
 // Error bits written to the caller-visible status word when a wait gives up.
 enum : int {
@@ -57,19 +72,23 @@ enum : int {
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int* status, uint64_t limit_ns = 2000000000ull) {
   if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = globaltimer_ns();
-  uint32_t spins = 0;
+  const uint64_t t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 63u) == 0) {
-      if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > limit_ns) {
-        *abort_flag = 1;
-        if (status) atomicOr(status, QMLA_DEV_ERR_TIMEOUT);
-        return false;
-      }
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > limit_ns) {
+      *abort_flag = 1;
+      if (status) atomicOr(status, QMLA_DEV_ERR_TIMEOUT);
+      return false;
     }
   }
+}
+
+// Fast 2^x (the hardware approximation, ~2 ulp; inputs here are <= 0 or small).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // ---------------------------------------------------------------- TMA
@@ -153,6 +172,16 @@ __device__ __forceinline__ void tc_mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, 
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D(tmem) (+)= A(smem desc) * B(smem desc), kind::f8f6f4 (both e4m3), fp32 accumulate.
+__device__ __forceinline__ void tc_mma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -178,6 +207,43 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const float* v) {
       "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
       "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
       : "memory");
+}
+
+// 16 lanes x 64 bit (half sub-partition): thread t reads lane base + 8*(t%2) + t/4,
+// 32-bit column 2*i + (t/2)%2 for i < N.
+template <int N>
+__device__ __forceinline__ void tmem_ld16x64(uint32_t taddr, float* v) {
+  uint32_t r[N];
+  if constexpr (N == 1) {
+    asm volatile("tcgen05.ld.sync.aligned.16x64b.x1.b32 {%0}, [%1];" : "=r"(r[0]) : "r"(taddr));
+  } else if constexpr (N == 2) {
+    asm volatile("tcgen05.ld.sync.aligned.16x64b.x2.b32 {%0,%1}, [%2];"
+                 : "=r"(r[0]), "=r"(r[1])
+                 : "r"(taddr));
+  } else if constexpr (N == 4) {
+    asm volatile("tcgen05.ld.sync.aligned.16x64b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr));
+  } else if constexpr (N == 8) {
+    asm volatile("tcgen05.ld.sync.aligned.16x64b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                   "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // ---------------------------------------------------------------- descriptors
