@@ -5,10 +5,11 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
-#include <mutex>
 #include <tuple>
+#include <mutex>
 
 #include "qmla.h"
 #include "qmla_aux.cuh"
@@ -56,16 +57,18 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-using MapKey = std::tuple<const void*, int, int, int, int64_t, int64_t, int64_t, int, int>;
+using MapKey = std::tuple<const void*, int, int, int, int64_t, int64_t, int64_t, int>;
 std::map<MapKey, CUtensorMap> g_maps;
 
-// 3-D map over the paged cache: (row element, token in page, page).  Each
-// box is one 128-byte column of `run` consecutive tokens of one page.
+// 3-D map over the paged cache: (row element, token in page, page).  Each box is
+// one 128-byte column of `run` consecutive tokens of one page.  The row extent is
+// the QK width, so columns past it (rms tail, padding) are zero-filled, and so are
+// pages outside [0, num_pages).
 int cache_tensor_map(const qmla_decode_params* p, int run, CUtensorMap* out) {
   const bool fp8 = p->kv_dtype == QMLA_DT_FP8E4M3;
   const int es = fp8 ? 1 : 2;
-  MapKey key{p->kv_cache, p->kv_dtype, p->kv_row_width, p->page_size, p->kv_num_pages,
-             p->kv_stride_page, p->kv_stride_token, run, 0};
+  MapKey key{p->kv_cache, p->kv_dtype, p->qk_dim, p->page_size, p->kv_num_pages,
+             p->kv_stride_page, p->kv_stride_token, run};
   {
     std::lock_guard<std::mutex> lk(g_mu);
     auto it = g_maps.find(key);
@@ -76,10 +79,8 @@ int cache_tensor_map(const qmla_decode_params* p, int run, CUtensorMap* out) {
   }
   auto fn = encode_fn();
   if (!fn) return QMLA_E_CUDA;
-  CUtensorMapDataType dt = fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
-                               : (p->kv_dtype == QMLA_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
-  cuuint64_t dims[3] = {(cuuint64_t)p->kv_row_width, (cuuint64_t)p->page_size,
+  CUtensorMapDataType dt = fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  cuuint64_t dims[3] = {(cuuint64_t)p->qk_dim, (cuuint64_t)p->page_size,
                         (cuuint64_t)p->kv_num_pages};
   cuuint64_t strides[2] = {(cuuint64_t)(p->kv_stride_token * es),
                            (cuuint64_t)(p->kv_stride_page * es)};
@@ -110,15 +111,16 @@ int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
 struct Plan {
   int npv, nb, nqk;
-  int n_slot_tile, n_qk_slots, n_sub_qk, fix_slot0;
-  int run;
+  int use_tma, run;
+  int n_qk_slots, n_sub_qk;
+  int qk_bytes, row_bytes;
+  int rms_bytes, rms_base_b, rms_units, rms_skip, pf_bytes;
   int G;
-  int rms_bytes;
   int q_vec, qpe_vec;
   // workspace offsets
   int64_t ws_status, ws_prefix, ws_plse, ws_po, ws_total;
   // smem
-  uint32_t off_ring, nslot, off_q, q_chunk, off_p, p_bytes, off_rms, off_misc;
+  uint32_t off_kring, nk, off_vring, nv, off_q, q_chunk, off_p, p_bytes, off_rms, off_misc;
   uint32_t smem_total;
 };
 
@@ -131,7 +133,7 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   const int nb = p->rank / 128;
   if (!(nb == 2 || nb == 3 || nb == 4 || nb == 6)) return QMLA_E_UNSUPPORTED;
   if (p->qk_dim < p->rank || p->qk_dim > 1024) return QMLA_E_UNSUPPORTED;
-  if (p->page_size <= 0 || p->page_size % 16 != 0) return QMLA_E_UNSUPPORTED;
+  if (p->page_size <= 0) return QMLA_E_INVALID;
   if (p->q_dtype != QMLA_DT_BF16 && p->q_dtype != QMLA_DT_F16) return QMLA_E_UNSUPPORTED;
   if (p->o_dtype < 0 || p->o_dtype > 2) return QMLA_E_UNSUPPORTED;
   if (p->lse && (p->lse_dtype < 0 || p->lse_dtype > 2)) return QMLA_E_UNSUPPORTED;
@@ -143,30 +145,41 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   if (reinterpret_cast<uintptr_t>(p->kv_cache) % 16 != 0) return QMLA_E_ALIGNMENT;
   if ((p->kv_stride_token * es) % 16 != 0 || (p->kv_stride_page * es) % 16 != 0)
     return QMLA_E_ALIGNMENT;
-  if (p->kv_row_width < p->qk_dim) return QMLA_E_INVALID;
+  if (p->kv_row_width < p->qk_dim || p->kv_stride_token < p->kv_row_width) return QMLA_E_INVALID;
 
   pl->nb = nb;
   pl->nqk = p->num_heads <= 16 ? 16 : p->num_heads <= 24 ? 24 : 32;
   pl->npv = pl->nqk <= 16 ? 16 : 32;
+  // Pages holding whole runs of 16 tokens are loaded with TMA boxes (no shared
+  // memory staging through L1); other page sizes with 16-byte cp.async gathers.
   pl->run = gcd_int(p->page_size, kTile);
+  pl->use_tma = pl->run >= 16 ? 1 : 0;
+  if (getenv("QMLA_NO_TMA")) pl->use_tma = 0;  // test hook: force the cp.async path
+  pl->qk_bytes = p->qk_dim * es;
+  pl->row_bytes = p->kv_row_width * es;
+  // rms tail: bf16 values (bf16 cache, or FP8 cache in BF16 mode), else one byte per head
   pl->rms_bytes = p->rms_mode == QMLA_RMS_NONE ? 0
-                  : p->rms_mode == QMLA_RMS_BF16 ? 2 * p->num_heads
-                                                 : p->num_heads;
-  const int rms_end = p->rms_mode == QMLA_RMS_NONE ? 0 : p->rms_offset + pl->rms_bytes;
-  if (p->rms_mode != QMLA_RMS_NONE && (p->rms_offset < p->qk_dim || rms_end > p->kv_row_width))
-    return QMLA_E_INVALID;
+                  : (!fp8 || p->rms_mode == QMLA_RMS_BF16) ? 2 * p->num_heads
+                                                           : p->num_heads;
+  pl->rms_base_b = pl->rms_units = pl->rms_skip = 0;
+  if (p->rms_mode != QMLA_RMS_NONE) {
+    const int64_t off_b = (int64_t)p->rms_offset * es;
+    if (p->rms_offset < p->qk_dim || off_b + pl->rms_bytes > pl->row_bytes) return QMLA_E_INVALID;
+    pl->rms_base_b = (int)(off_b & ~int64_t(15));
+    pl->rms_skip = (int)(off_b - pl->rms_base_b);
+    pl->rms_units = (pl->rms_skip + pl->rms_bytes + 15) / 16;
+    if (pl->rms_units > kRmsMaxUnits) return QMLA_E_UNSUPPORTED;
+  }
+  {
+    // L2 prefetch span of a row: the QK columns and the rms tail, in 16-byte units
+    int64_t end = pl->qk_bytes;
+    if (pl->rms_units) end = std::max<int64_t>(end, pl->rms_base_b + 16 * pl->rms_units);
+    end = std::min<int64_t>(align_up(end, 16), p->kv_stride_token * es);
+    pl->pf_bytes = (int)end;
+  }
   // slots are 128 dims (elements of a bf16 row, bytes of an FP8 row)
-  pl->n_slot_tile = (std::max(p->qk_dim, rms_end) + 127) / 128;
   pl->n_qk_slots = (p->qk_dim + 127) / 128;
   pl->n_sub_qk = fp8 ? pl->n_qk_slots : (p->qk_dim + 63) / 64;
-  pl->fix_slot0 = -1;
-  if (fp8) {
-    int lo = 1 << 30;
-    if (p->qk_dim % 128 != 0) lo = p->qk_dim;
-    if (p->rms_mode != QMLA_RMS_NONE) lo = std::min(lo, p->rms_offset);
-    if (lo < (1 << 30)) pl->fix_slot0 = lo / 128;
-    if (pl->rms_bytes > 64) return QMLA_E_UNSUPPORTED;
-  }
   if (pl->n_sub_qk > kMaxQkChunks) return QMLA_E_UNSUPPORTED;
   if (pl->n_qk_slots < nb) return QMLA_E_INVALID;
   // 16-byte vector loads of q rows (bf16 only; element strides in 2-byte units)
@@ -185,23 +198,40 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   G = std::min(G, kMaxCtas);
   pl->G = G;
 
-  // shared memory map
+  // shared memory map: K ring, V ring, Q, 2 P buffers, 2 rms staging buffers, misc
   const uint32_t slot_bytes = fp8 ? 8192u : 16384u;
   const int q_rows = fp8 ? 2 * pl->nqk : pl->nqk;
   pl->q_chunk = (uint32_t)((q_rows + 7) / 8 * 1024);
   const uint32_t q_bytes = pl->q_chunk * pl->n_sub_qk;
   pl->p_bytes = (uint32_t)(pl->npv * 128);
-  const uint32_t misc_bytes = 3072;
-  const uint32_t rms_smem = fp8 ? 2 * kTile * 64 : 0;
+  const uint32_t misc_bytes = 4096;
+  const uint32_t rms_smem = pl->rms_units ? 2 * kTile * kRmsStride : 0;
   const uint32_t fixed = q_bytes + 2 * pl->p_bytes + misc_bytes + rms_smem + 1024 /*align slack*/;
   const int budget = std::min(di.max_smem, kMaxDynSmem) - (int)fixed;
   const int ns = budget / (int)slot_bytes;
-  if (ns < pl->n_slot_tile) return QMLA_E_UNSUPPORTED;
-  pl->nslot = (uint32_t)std::min(ns, 3 * pl->n_slot_tile);
-  if ((2 * pl->nslot + 21) * 8 + 16 + 1536 > misc_bytes) return QMLA_E_UNSUPPORTED;
+  if (ns < 2) return QMLA_E_UNSUPPORTED;
+  // K ring: the HBM stream (bandwidth x latency); V ring: L2 re-reads for PV
+  int nk = std::max(1, std::min((ns * 11 + 19) / 20, 3 * pl->n_qk_slots));
+  // A PV issuer skips the other issuer's blocks of each tile, so it may wait on a
+  // V slot up to max(NB0, NB - NB0) positions after the last one it saw filled;
+  // one more slot than that keeps every parity wait within one phase.
+  const int nb0 = (nb + 1) / 2;
+  const int nv_min = std::max(nb0, nb - nb0) + 1;
+  int nv = std::max(nv_min, std::min(ns - nk, 2 * nb));
+  // test hooks: QMLA_NK / QMLA_NV override the ring sizes (clamped to legal values)
+  if (const char* e = getenv("QMLA_NK")) nk = std::max(1, std::min(atoi(e), ns - nv_min));
+  nv = std::max(nv_min, std::min(nv, ns - nk));
+  if (const char* e = getenv("QMLA_NV")) nv = std::max(nv_min, std::min(atoi(e), ns - nk));
+  if (nk + nv > ns) return QMLA_E_UNSUPPORTED;
+  pl->nk = (uint32_t)nk;
+  pl->nv = (uint32_t)nv;
+  const uint32_t n_bars = 2 * (pl->nk + pl->nv) + 14 + kKdoneDepth + 4;
+  if ((n_bars * 8 + 15) / 16 * 16 + 16 + 1024 + 512 + 1024 > misc_bytes) return QMLA_E_UNSUPPORTED;
   uint32_t off = 0;
-  pl->off_ring = off;
-  off += pl->nslot * slot_bytes;
+  pl->off_kring = off;
+  off += pl->nk * slot_bytes;
+  pl->off_vring = off;
+  off += pl->nv * slot_bytes;
   pl->off_q = off;
   off += q_bytes;
   pl->off_p = off;
@@ -236,7 +266,7 @@ int launch_decode_t(const CUtensorMap& tmap, const DecodeArgs& a, uint32_t smem,
     attr_err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
   });
   if (attr_err != cudaSuccess) return QMLA_E_CUDA;
-  k<<<a.G, FP8 ? 384 : 352, smem, st>>>(tmap, a);
+  k<<<a.G, kNumThreads, smem, st>>>(tmap, a);
   return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
 }
 
@@ -300,7 +330,7 @@ const char* qmla_error_string(int code) {
     case QMLA_E_UNSUPPORTED:
       return "unsupported shape or dtype";
     case QMLA_E_ALIGNMENT:
-      return "pointer or stride not 16-byte aligned for TMA";
+      return "pointer or stride not 16-byte aligned";
     case QMLA_E_WORKSPACE:
       return "workspace too small";
     case QMLA_E_CUDA:
@@ -348,19 +378,28 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
   a.bt_stride = p->block_table_stride;
   a.seq_lens = p->seq_lens;
   a.page_size = p->page_size;
+  a.use_tma = pl.use_tma;
   a.run_rows = pl.run;
+  a.cache = reinterpret_cast<const uint8_t*>(p->kv_cache);
+  {
+    const int es = p->kv_dtype == QMLA_DT_FP8E4M3 ? 1 : 2;
+    a.page_stride_b = p->kv_stride_page * es;
+    a.token_stride_b = p->kv_stride_token * es;
+    a.num_pages = p->kv_num_pages;
+  }
   a.num_rows = p->num_rows;
   a.H = p->num_heads;
   a.rank = p->rank;
   a.qk_dim = p->qk_dim;
-  a.rms_offset = p->rms_offset;
   a.rms_mode = p->rms_mode;
-  a.rms_bytes = pl.rms_bytes;
-  a.nqk = pl.nqk;
-  a.n_slot_tile = pl.n_slot_tile;
+  a.qk_bytes = pl.qk_bytes;
+  a.row_bytes = pl.row_bytes;
   a.n_qk_slots = pl.n_qk_slots;
   a.n_sub_qk = pl.n_sub_qk;
-  a.fix_slot0 = pl.fix_slot0;
+  a.rms_base_b = pl.rms_base_b;
+  a.rms_units = pl.rms_units;
+  a.rms_skip = pl.rms_skip;
+  a.pf_bytes = pl.pf_bytes;
   a.sm_scale = p->sm_scale;
   a.logit_cap = p->logit_cap;
   a.k_scale = p->k_scale;
@@ -377,8 +416,10 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
   a.part_lse = reinterpret_cast<float*>(ws + pl.ws_plse);
   a.part_o = reinterpret_cast<float*>(ws + pl.ws_po);
   a.G = pl.G;
-  a.off_ring = pl.off_ring;
-  a.nslot = pl.nslot;
+  a.off_kring = pl.off_kring;
+  a.nk = pl.nk;
+  a.off_vring = pl.off_vring;
+  a.nv = pl.nv;
   a.off_q = pl.off_q;
   a.q_chunk_bytes = pl.q_chunk;
   a.off_p = pl.off_p;
@@ -393,9 +434,11 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
 
   if (p->num_rows == 0) return QMLA_OK;
   CUtensorMap tmap;
-  rc = cache_tensor_map(p, pl.run, &tmap);
-  if (rc != QMLA_OK) return rc;
-
+  memset(&tmap, 0, sizeof(tmap));
+  if (pl.use_tma) {
+    rc = cache_tensor_map(p, pl.run, &tmap);
+    if (rc != QMLA_OK) return rc;
+  }
   if (!p->plan_tile_prefix) {
     plan_kernel<<<1, 1024, 0, st>>>(p->seq_lens, p->num_rows,
                                     reinterpret_cast<int32_t*>(ws + pl.ws_prefix), a.status);

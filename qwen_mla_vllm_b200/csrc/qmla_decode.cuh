@@ -2,26 +2,29 @@
 //
 // One persistent CTA per SM walks a balanced, contiguous range of 64-token
 // tiles over all decode rows (rows are cut into segments at CTA boundaries and
-// merged afterwards).  Warp roles:
+// merged afterwards).  Warp roles (16 warps, 512 threads):
 //   warps 0-7   softmax / epilogue.  Warp w reads TMEM sub-partition w%4 and
-//               owns half of the heads (w/4); all 32 lanes are busy (two lanes
-//               per token, alternate heads, via the 16x64b TMEM load shape)
-//   warp  8     TMA producer: page-table lookups + 3-D tiled bulk loads
-//   warp  9     QK issuer (tcgen05) + TMEM owner
-//   warp  10    PV issuer (tcgen05)
-//   warp  11    (FP8 cache) rms-tail fix-up: copies the per-head rms bytes out
-//               of the tile and zeroes the bytes between the attention width
-//               and the MMA K boundary, so log8 codes never reach the MMA
+//               owns half of the heads (w/4); two lanes per token, alternate
+//               heads (16x64b TMEM loads), so all 32 lanes are busy
+//   warps 8-10  K loads: 16-byte cp.async gathers of each tile's QK columns
+//               from the paged cache into the K ring (zero-filled past the
+//               attention width and past the row end), plus the tile's rms tail
+//               into a small staging buffer
+//   warp  11    V loads: re-reads the tile's latent columns (L2-resident by then)
+//               into the V ring once QK of the tile has finished
+//   warps 12-13 QK issuers (tcgen05), one S partial each; warp 12 owns TMEM
+//   warps 14-15 PV issuers (tcgen05), about half of the 128-dim output blocks each
 // Per 64-token tile:
 //   S^T[64 tok, heads] = K_tile . Q^T      tcgen05 M=64, K-major A and B
 //   softmax over tokens with the per-(token, head) rms divisor, base 2, lazy
 //   rescale (O is only rescaled when a running max grows by more than 2^8)
 //   O^T[rank, heads]  += V^T . P^T         tcgen05 M=128, MN-major A and B
-// bf16 caches use kind::f16 (bf16 operands).  FP8 caches use kind::f8f6f4 on
-// the raw e4m3 tile; q and P are each split into two e4m3 terms (hi + lo)
-// stacked along N, so the contraction keeps ~bf16 precision without any
-// dequantisation pass over the cache.  The latent part of a tile stays in
-// shared memory from QK to PV, so each cache byte crosses HBM once.
+// K slots are freed as soon as their QK MMAs complete, so the HBM stream never
+// waits for the softmax.  bf16 caches use kind::f16.  FP8 caches use
+// kind::f8f6f4 on the raw e4m3 tile; q and P are each split into two e4m3 terms
+// (hi + lo): q's terms are stacked along N of the QK MMA (summed by the
+// softmax), P's terms are two PV MMAs into the same accumulator.  That keeps
+// ~bf16 precision without a dequantisation pass over the cache.
 // Semantics follow the reference Triton kernel
 // qwen_mla/ops/mla_decode_attention.py:297-586 and its split merge :1064-1137.
 #pragma once
@@ -39,11 +42,21 @@ constexpr int kMaxQkChunks = 16;   // QK width <= 1024 elements
 constexpr int kMaxCtas = 160;      // persistent CTAs per launch (B200: 148 SMs)
 constexpr int kSoftmaxWarps = 8;
 constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
-constexpr int kWarpProducer = 8, kWarpQK = 9, kWarpPV = 10, kWarpFix = 11;
+constexpr int kWarpK = 8, kNumKWarps = 3, kWarpV = 11, kWarpQK = 12, kWarpPV = 14;
+constexpr int kNumWarps = 16, kNumThreads = kNumWarps * 32;
+constexpr int kKThreads = kNumKWarps * 32;
+constexpr int kRmsStride = 80;     // staging bytes per token: <= 64 rms bytes + 16-byte alignment
+constexpr int kRmsMaxUnits = kRmsStride / 16;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P may reach 2^8 before O is rescaled
 constexpr int kBarSoftmax = 1;             // named barrier id of the softmax warps
+constexpr int kBarK = 2;                   // named barrier id of the K-load warps
+constexpr int kKdoneDepth = 8;             // QK-done signals in flight (V loads trail QK)
+#ifndef QMLA_PREFETCH_TILES
+#define QMLA_PREFETCH_TILES 2
+#endif
+constexpr int kPrefetchTiles = QMLA_PREFETCH_TILES;  // tiles of a row prefetched into L2 ahead
 
 struct DecodeArgs {
   // query
@@ -53,18 +66,24 @@ struct DecodeArgs {
   int q_dtype;
   int q_vec, qpe_vec;  // 16-byte vector loads are legal for q / q_pe rows
   // cache / paging
+  const uint8_t* cache;
+  int64_t page_stride_b, token_stride_b, num_pages;
   const int32_t* block_table;
   int64_t bt_stride;
   const int32_t* seq_lens;
   int page_size;
-  int run_rows;  // gcd(page_size, 64): tokens per TMA box
+  int use_tma;   // 1: K tiles by 3-D TMA boxes of run_rows tokens (page_size % 16 == 0)
+  int run_rows;  // tokens per TMA box: gcd(page_size, 64)
   // geometry
-  int num_rows, H, rank, qk_dim, rms_offset, rms_mode, rms_bytes;
-  int nqk;          // heads rounded up to a multiple of 8
-  int n_slot_tile;  // 128-dim slots loaded per tile (covers qk and the rms tail)
-  int n_qk_slots;   // slots the QK contraction reads
+  int num_rows, H, rank, qk_dim, rms_mode;
+  int qk_bytes;     // bytes of a cache row the QK contraction reads
+  int row_bytes;    // bytes of a cache row (kv_row_width * element size)
+  int n_qk_slots;   // 128-dim slots loaded per tile
   int n_sub_qk;     // 128-byte-wide MMA sub-chunks of the QK width
-  int fix_slot0;    // FP8: first slot the fix-up reads (-1: none)
+  int rms_base_b;   // 16-byte-aligned first byte of the rms tail in a row
+  int rms_units;    // 16-byte units staged per token (0: no rms)
+  int rms_skip;     // first rms byte within the staged units
+  int pf_bytes;     // bytes of a cache row prefetched into L2 (QK columns + rms tail)
   float sm_scale;
   float logit_cap;
   const float* k_scale;
@@ -82,20 +101,28 @@ struct DecodeArgs {
   float* part_lse;             // [2*G][H] (log2 units)
   int G;
   // shared-memory layout (byte offsets from the 1024-aligned base)
-  uint32_t off_ring, nslot, off_q, q_chunk_bytes, off_p, p_bytes, off_rms, off_misc;
+  uint32_t off_kring, nk, off_vring, nv, off_q, q_chunk_bytes, off_p, p_bytes, off_rms, off_misc;
   // Optional stage timestamps of CTA 0 (builds with -DQMLA_TRACE only):
   // trace[tile * 16 + event] = %globaltimer in ns.
   unsigned long long* trace;
 };
 
 #ifdef QMLA_TRACE
-#define QMLA_TR(ev)                                                                 \
-  do {                                                                               \
+#define QMLA_TR(ev)                                                                            \
+  do {                                                                                         \
     if (a.trace && blockIdx.x == 0 && jt < 256) a.trace[jt * 16 + (ev)] = globaltimer_ns(); \
+  } while (0)
+#define QMLA_TRS(plane, idx)                                                     \
+  do {                                                                           \
+    if (a.trace && blockIdx.x == 0 && jt < 256)                                  \
+      a.trace[(plane) * 4096 + jt * 16 + (idx)] = globaltimer_ns();              \
   } while (0)
 #else
 #define QMLA_TR(ev) \
   do {              \
+  } while (0)
+#define QMLA_TRS(plane, idx) \
+  do {                       \
   } while (0)
 #endif
 
@@ -184,34 +211,54 @@ __device__ __forceinline__ void load_s_pairs(uint32_t taddr, float* v) {
   }
 }
 
+// Slot index and phase bit of a sequentially used mbarrier ring.
+struct Ring {
+  uint32_t idx = 0, ph = 0;
+  __device__ __forceinline__ void next(uint32_t n) {
+    if (++idx == n) {
+      idx = 0;
+      ph ^= 1;
+    }
+  }
+};
+
+// Cache-row address of token t (0..63) of tile k of a row; 0 past the row end
+// or for a page id outside the cache (those rows are zero-filled, never read).
+__device__ __forceinline__ uint64_t token_row_addr(const DecodeArgs& a, const int32_t* bt, int L,
+                                                   int k, int t) {
+  const int tok = k * kTile + t;
+  if (tok >= L) return 0ull;
+  const int pg = __ldg(bt + tok / a.page_size);
+  if (pg < 0 || pg >= a.num_pages) return 0ull;
+  return reinterpret_cast<uint64_t>(a.cache + (int64_t)pg * a.page_stride_b +
+                                    (int64_t)(tok % a.page_size) * a.token_stride_b);
+}
+
 // ---------------------------------------------------------------- the kernel
 template <bool FP8, int NB, int NQK>
-__global__ void __launch_bounds__(FP8 ? 384 : 352, 1)
+__global__ void __launch_bounds__(kNumThreads, 1)
     mla_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
   static_assert(NQK % 8 == 0 && NQK >= 8 && NQK <= 32, "heads rounded to 8..32");
-  constexpr int NPV = NQK <= 16 ? 16 : 32;  // PV MMA N (multiple of 16)
+  constexpr int NPV = NQK <= 16 ? 16 : 32;        // PV MMA N (multiple of 16)
   constexpr int kSlotBytes = FP8 ? 8192 : 16384;  // 64 tokens x 128 dims
   constexpr int kSubs = FP8 ? 1 : 2;              // 128-byte-wide sub-chunks per slot
-  constexpr int OW = FP8 ? 2 * NPV : NPV;         // TMEM columns per O block (hi|lo for FP8)
+  constexpr int kUnitsPerRow = kSubs * 8;         // 16-byte units per token per slot
+  constexpr int OW = NPV;                         // TMEM columns per O block
   constexpr int SWP = FP8 ? 2 * NPV : NPV;        // TMEM columns per S partial (hi|lo for FP8)
-  // Consecutive MMAs into one accumulator serialise (~64 cycles each); independent
-  // accumulators pipeline down to the operand-fetch bound.  So the QK reduction is
-  // split over KP partial accumulators (summed by the softmax) and S is double
-  // buffered (SB) when TMEM allows.
-  constexpr int kFree = 512 - NB * OW;
-  constexpr int KP = (kFree >= 8 * SWP) ? 4 : (kFree >= 4 * SWP) ? 2 : (kFree >= 2 * SWP) ? 2 : 1;
-  constexpr int SB = (kFree >= 2 * KP * SWP) ? 2 : 1;
-  constexpr int SW = KP * SWP;                     // TMEM columns per S buffer
+  constexpr int KP = 2;                           // S partials (one per QK issuer)
+  constexpr int SB = 2;                           // S buffers
+  constexpr int SW = KP * SWP;                    // TMEM columns per S buffer
   constexpr uint32_t kCols = NB * OW + SB * SW;
   constexpr uint32_t kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128
                                  : kCols <= 256 ? 256 : 512;
   static_assert(kCols <= 512, "TMEM budget");
   constexpr int NJ = NQK / 4;   // heads per softmax thread
   constexpr int NJP = NPV / 4;  // P^T columns per softmax thread (NJ real + zero padding)
-  constexpr int kKStepBytes = 32;
-  constexpr int kPvSteps = FP8 ? 2 : 4;      // K = 32 (e4m3) or 16 (bf16) tokens per PV MMA
+  constexpr int kPvSteps = FP8 ? 2 : 4;  // K = 32 (e4m3) or 16 (bf16) tokens per PV MMA
   constexpr int kPvAStep = FP8 ? 4096 : 2048;
   constexpr int kPvBStep = (FP8 ? 4 : 2) * 16 * NPV;
+  constexpr int kKTokStep = kKThreads / kUnitsPerRow;  // tokens between a K thread's copies
+  constexpr int kKIters = (kTile + kKTokStep - 1) / kKTokStep;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -230,43 +277,50 @@ __global__ void __launch_bounds__(FP8 ? 384 : 352, 1)
 
   // ------------------------------------------------ barriers and scratch
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + a.off_misc);
-  const uint32_t nslot = a.nslot;
-  const uint32_t b_full = 0;                // [nslot] TMA landed
-  const uint32_t b_empty = nslot;           // [nslot] slot free
-  const uint32_t b_sfull = 2 * nslot;       // [2] S ready
-  const uint32_t b_sempty = b_sfull + 2;    // [2] S consumed
-  const uint32_t b_pfull = b_sempty + 2;    // [2] P written (+ O rescaled)
-  const uint32_t b_odone = b_pfull + 2;     // [2] PV finished
-  const uint32_t b_qfull = b_odone + 2;     // [1] Q staged
-  const uint32_t b_ofree = b_qfull + 1;     // [1] O read by the epilogue
-  const uint32_t b_fix = b_ofree + 1;       // [2] FP8 fix-up done (rms staged)
-  const uint32_t b_rempty = b_fix + 2;      // [2] FP8 rms staging consumed
-  const uint32_t b_fin = b_rempty + 2;      // [2] issuer drain at teardown
-  const uint32_t b_rdone = b_fin + 2;       // [2] bf16: rms tail of the tile read
-  const uint32_t n_bars = b_rdone + 2;
+  const uint32_t nk = a.nk, nv = a.nv;
+  const uint32_t b_kfull = 0;                    // [nk] K slot landed (cp.async arrivals)
+  const uint32_t b_kempty = nk;                  // [nk] K slot free (both QK issuers)
+  const uint32_t b_vfull = 2 * nk;               // [nv] V slot landed
+  const uint32_t b_vempty = 2 * nk + nv;         // [nv] V slot free
+  const uint32_t b_sfull = 2 * (nk + nv);        // [2] S ready (both QK issuers)
+  const uint32_t b_sempty = b_sfull + 2;         // [2] S consumed
+  const uint32_t b_pfull = b_sempty + 2;         // [2] P written (+ O rescaled)
+  const uint32_t b_odone = b_pfull + 2;          // [2] PV finished (both PV issuers)
+  const uint32_t b_rfull = b_odone + 2;          // [2] rms tail staged
+  const uint32_t b_rempty = b_rfull + 2;         // [2] rms staging consumed
+  const uint32_t b_qfull = b_rempty + 2;         // [1] Q staged
+  const uint32_t b_ofree = b_qfull + 1;          // [1] O read by the epilogue
+  const uint32_t b_kdone = b_ofree + 1;          // [kKdoneDepth] QK of a tile finished
+  const uint32_t b_fin = b_kdone + kKdoneDepth;  // [4] issuer drain at teardown
+  const uint32_t n_bars = b_fin + 4;
   auto bar = [&](uint32_t i) -> uint32_t { return smem_u32(bars + i); };
   uint8_t* misc2 = smem + a.off_misc + ((n_bars * 8 + 15) / 16) * 16;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc2);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc2 + 4);
-  float* red = reinterpret_cast<float*>(misc2 + 16);   // [2 halves][4 sp][32]
-  float* hv = red + 256;                               // [4][32] per-head broadcast values
+  float* red = reinterpret_cast<float*>(misc2 + 16);  // [2 halves][4 sp][32]
+  float* hv = red + 256;                              // [4][32] per-head broadcast values
   // hv[0..31] alpha, hv[32..63] l, hv[64..95] m, hv[96..127] q scale (FP8)
+  uint64_t* tokptr = reinterpret_cast<uint64_t*>(hv + 128);  // [2][64] K-load row addresses
 
   if (threadIdx.x == 0) {
-    for (uint32_t i = 0; i < nslot; ++i) {
-      mbar_init(bar(b_full + i), 1);
-      mbar_init(bar(b_empty + i), 1);
+    for (uint32_t i = 0; i < nk; ++i) {
+      mbar_init(bar(b_kfull + i), a.use_tma ? 1 : kKThreads);
+      mbar_init(bar(b_kempty + i), KP);
+    }
+    for (uint32_t i = 0; i < nv; ++i) {
+      mbar_init(bar(b_vfull + i), 32);
+      mbar_init(bar(b_vempty + i), 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(bar(b_sfull + i), 1);
+      mbar_init(bar(b_sfull + i), KP);
       mbar_init(bar(b_sempty + i), kSoftmaxWarps);
       mbar_init(bar(b_pfull + i), kSoftmaxWarps);
-      mbar_init(bar(b_odone + i), 1);
-      mbar_init(bar(b_fix + i), 1);
+      mbar_init(bar(b_odone + i), 2);
+      mbar_init(bar(b_rfull + i), a.use_tma ? kKThreads - 32 : kKThreads);
       mbar_init(bar(b_rempty + i), kSoftmaxWarps);
-      mbar_init(bar(b_fin + i), 1);
-      mbar_init(bar(b_rdone + i), kSoftmaxWarps);
     }
+    for (int i = 0; i < kKdoneDepth; ++i) mbar_init(bar(b_kdone + i), KP);
+    for (int i = 0; i < 4; ++i) mbar_init(bar(b_fin + i), 1);
     mbar_init(bar(b_qfull), kSoftmaxWarps);
     mbar_init(bar(b_ofree), kSoftmaxWarps);
     *abort_flag = 0;
@@ -276,7 +330,6 @@ __global__ void __launch_bounds__(FP8 ? 384 : 352, 1)
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish();
   }
-  if (warp == kWarpProducer && lane == 0) prefetch_tmap(&tmap);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -284,298 +337,394 @@ __global__ void __launch_bounds__(FP8 ? 384 : 352, 1)
   const uint32_t col_o = 0;
   const uint32_t col_s = NB * OW;
 
-  const uint32_t ring = sbase + a.off_ring;
+  const uint32_t kring = sbase + a.off_kring;
+  const uint32_t vring = sbase + a.off_vring;
   const uint32_t qbuf = sbase + a.off_q;
   const uint32_t pbuf = sbase + a.off_p;
+  const uint32_t rmsbuf = sbase + a.off_rms;  // [2][64 tokens][kRmsStride]
   int* status = a.status;
-  auto slot_addr = [&](uint32_t it) -> uint32_t { return ring + (it % nslot) * kSlotBytes; };
-  // Tile-local load order: the rope / rms slots (dims slots >= NB) first, then the
-  // latent slots.  Rope slots are released as soon as S (and the rms tail) are
-  // consumed, so the next tile's first loads can start while this tile's latent
-  // part is still held for PV.
-  const int nrope = a.n_slot_tile - NB;
-  auto pos_of = [&](int s) -> int { return s >= NB ? s - NB : nrope + s; };
-  auto dims_of = [&](int t) -> int { return t < nrope ? NB + t : t - nrope; };
-  // shared address of tile-local position t given the tile's first ring index
-  auto slot_at = [&](uint32_t tbase, int t) -> uint32_t {
-    uint32_t idx = tbase + (uint32_t)t;
-    if (idx >= nslot) idx -= nslot;
-    return ring + idx * kSlotBytes;
-  };
 
-  if (warp == kWarpProducer) {
-    // ====================================================== TMA producer
-    const uint64_t pol = policy_evict_first();
-    const int runs = kTile / a.run_rows;  // 1, 2 or 4
-    const int xstep = FP8 ? 128 : 64;     // box width in elements
+  if (a.use_tma && warp == kWarpK) {
+    // ====================================================== K loads by TMA
+    // Per 128-dim slot: one box per (128-byte column, run of tokens within a page);
+    // lanes issue the boxes of a slot side by side.  Columns past the QK width
+    // and pages outside the cache are zero-filled by the tensor map bounds.
+    const uint64_t pol_lat = policy_evict_normal();
+    const uint64_t pol_rope = policy_evict_first();
+    const int run = a.run_rows, nrun = kTile / run, nbox = kSubs * nrun;
+    const int xstep = FP8 ? 128 : 64;  // box width in elements
+    const int bsc = lane / nrun, bg = lane % nrun;  // this lane's box: sub-chunk, token run
+    if (lane == 0) prefetch_tmap(&tmap);
     SegCursor cur{row0, range_lo, range_hi};
     int row, k0, k1, plo, phi;
-    uint32_t jt = 0, armed = 0, ridx = 0, rph = 0;
+    uint32_t jt = 0, armed = 0;
+    Ring r;
     bool ok = true;
     while (ok && next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi)) {
       int L = __ldg(a.seq_lens + row);
       L = L < 0 ? 0 : L;
       const int32_t* bt = a.block_table + (int64_t)row * a.bt_stride;
-      auto page_of = [&](int k, int& y) -> int {
-        int tok0 = k * kTile + lane * a.run_rows;
-        y = 0;
-        if (lane < runs && tok0 < L) {
-          y = tok0 % a.page_size;
-          return __ldg(bt + tok0 / a.page_size);
-        }
-        return -1;  // out of the tensor: TMA fills zeros
-      };
-      int ny, npage = page_of(k0, ny);
       for (int k = k0; k < k1 && ok; ++k, ++jt) {
-        int cpage = npage, cy = ny;
-        if (k + 1 < k1) npage = page_of(k + 1, ny);  // prefetch next tile's pages
-        int pages[4], ys[4];
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          pages[r] = __shfl_sync(0xffffffffu, cpage, r);
-          ys[r] = __shfl_sync(0xffffffffu, cy, r);
+        int pg = -1;  // page of token run `lane`; runs past the row end load zeros
+        if (lane < nrun) {
+          const int tok = k * kTile + lane * run;
+          if (tok < L) pg = __ldg(bt + tok / a.page_size);
         }
-        for (int t = 0; t < a.n_slot_tile && ok; ++t) {
-          const int s = dims_of(t);
+        const int mypg = __shfl_sync(0xffffffffu, pg, bg);
+        const int y = (k * kTile + bg * run) % a.page_size;
+        for (int s = 0; s < a.n_qk_slots && ok; ++s) {
           if (lane == 0) {
-            ok = mbar_wait(bar(b_empty + ridx), rph ^ 1, abort_flag, status);
-            if (t == 0) QMLA_TR(0);
-            if (ok) {
-              const uint32_t fb = bar(b_full + ridx);
-              mbar_expect_tx(fb, (uint32_t)kSlotBytes);
-              const uint32_t dst0 = ring + ridx * kSlotBytes;
-#pragma unroll
-              for (int sc = 0; sc < kSubs; ++sc)
-                for (int r = 0; r < runs; ++r)
-                  tma_load_3d(dst0 + sc * 8192 + r * a.run_rows * 128, &tmap, (kSubs * s + sc) * xstep,
-                              ys[r], pages[r], fb, pol);
-              armed = jt * a.n_slot_tile + t + 1;
-              if (t == a.n_slot_tile - 1) QMLA_TR(1);
-              if (t == 0) QMLA_TR(13);
-            }
-          }
-          if (++ridx == nslot) {
-            ridx = 0;
-            rph ^= 1;
+            ok = mbar_wait(bar(b_kempty + r.idx), r.ph ^ 1, abort_flag, status);
+            if (ok) mbar_expect_tx(bar(b_kfull + r.idx), (uint32_t)kSlotBytes);
+            QMLA_TRS(4, s);
+            if (s == 0) QMLA_TR(0);
           }
           ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (ok) {
+            if (lane < nbox)
+              tma_load_3d(kring + r.idx * kSlotBytes + bsc * 8192 + bg * run * 128, &tmap,
+                          (kSubs * s + bsc) * xstep, y, mypg, bar(b_kfull + r.idx),
+                          s < NB ? pol_lat : pol_rope);
+            ++armed;
+          }
+          if (lane == 0) QMLA_TRS(1, s);
+          r.next(nk);
         }
       }
     }
-    // After an abort: wait (bounded) for the loads already issued so no bulk
-    // copy still targets this CTA's shared memory when it exits.
+    // After an abort: wait (bounded) for the boxes already issued, so no copy still
+    // targets this CTA's shared memory when it exits.
     if (!ok && lane == 0) {
-      uint32_t first = armed > nslot ? armed - nslot : 0u;
-      for (uint32_t it = first; it < armed; ++it) {
+      for (uint32_t p = armed > nk ? armed - nk : 0u; p < armed; ++p) {
         volatile int never = 0;
-        mbar_wait(bar(b_full + it % nslot), (it / nslot) & 1, &never, nullptr, 20000000ull);
+        mbar_wait(bar(b_kfull + p % nk), (p / nk) & 1, &never, nullptr, 20000000ull);
       }
     }
-  } else if (warp == kWarpQK) {
-    // ====================================================== QK issuer
-    const uint32_t idesc = FP8 ? make_idesc_f16(0, 64, 2 * NQK, 0, 0)
-                               : make_idesc_f16(1, 64, NQK, 0, 0);
-    const uint32_t qc16 = a.q_chunk_bytes >> 4;               // Q chunk stride, descriptor units
-    const uint64_t q_desc0 = make_sdesc(qbuf, 16, 1024, 2);   // Q chunk 0 (K-major, 128B swizzle)
-    const int fix_slot = (FP8 && a.fix_slot0 >= 0) ? a.fix_slot0 : 1 << 30;
+    __syncwarp();
+  } else if (a.use_tma && warp > kWarpK && warp < kWarpK + kNumKWarps) {
+    // ====================================================== rms tail + L2 prefetch (TMA mode)
+    const int pt = threadIdx.x - (kWarpK + 1) * 32;  // 0..63: one token of the tile each
+    const uint64_t pol_lat = policy_evict_normal();
+    const uint64_t pol_rope = policy_evict_first();
     SegCursor cur{row0, range_lo, range_hi};
     int row, k0, k1, plo, phi;
-    uint32_t jt = 0, sidx = 0, ridx = 0, rph = 0;
+    uint32_t jt = 0;
     bool ok = true;
     while (ok && next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi)) {
-      if (lane == 0) ok = mbar_wait(bar(b_qfull), sidx & 1, abort_flag, status);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
+      int L = __ldg(a.seq_lens + row);
+      L = L < 0 ? 0 : L;
+      const int32_t* bt = a.block_table + (int64_t)row * a.bt_stride;
+      for (int kp = k0; kp < min(k1, k0 + kPrefetchTiles); ++kp) {
+        const uint64_t pa = token_row_addr(a, bt, L, kp, pt);
+        if (pa) bulk_prefetch_l2(reinterpret_cast<const void*>(pa), a.pf_bytes, pol_lat);
+      }
       for (int k = k0; k < k1 && ok; ++k, ++jt) {
-        const uint32_t sb = jt % SB;
-        const uint32_t pb = jt & 1;
-        if (lane == 0) {
-          if (jt >= SB) ok = mbar_wait(bar(b_sempty + sb), ((jt - SB) / SB) & 1, abort_flag, status);
-          QMLA_TR(2);
-          tc_fence_after();
-          const uint32_t d_s = tmem_base + col_s + sb * SW;
-          bool first = true;  // first sub-chunk of the tile initialises the KP partials
-          for (int t = 0; t < a.n_slot_tile; ++t) {
-            const int s = dims_of(t);
-            const uint32_t cidx = ridx, cph = rph;
-            if (++ridx == nslot) {
-              ridx = 0;
-              rph ^= 1;
+        if (k + kPrefetchTiles < k1) {
+          const uint64_t pa = token_row_addr(a, bt, L, k + kPrefetchTiles, pt);
+          if (pa) bulk_prefetch_l2(reinterpret_cast<const void*>(pa), a.pf_bytes, pol_lat);
+        }
+        if (a.rms_units > 0) {
+          const uint32_t tb = jt & 1;
+          if (jt >= 2) ok = mbar_wait(bar(b_rempty + tb), ((jt - 2) >> 1) & 1, abort_flag, status);
+          if (ok) {
+            const uint64_t src = token_row_addr(a, bt, L, k, pt);
+            for (int u = 0; u < a.rms_units; ++u) {
+              const int col = a.rms_base_b + 16 * u;
+              const int nbytes = src ? max(0, min(16, a.row_bytes - col)) : 0;
+              cp_async_16_hint(rmsbuf + tb * (kTile * kRmsStride) + pt * kRmsStride + 16 * u,
+                               nbytes ? reinterpret_cast<const void*>(src + col) : a.cache,
+                               (uint32_t)nbytes, pol_rope);
             }
-            if (!ok || s >= a.n_qk_slots) continue;  // rms-only slot (ring position still advances)
-            if (s == fix_slot) ok = mbar_wait(bar(b_fix + pb), (jt >> 1) & 1, abort_flag, status);
-            if (ok) ok = mbar_wait(bar(b_full + cidx), cph, abort_flag, status);
-            if (!ok) continue;
-            if (t == 0) QMLA_TR(3);
-            if (t == a.n_slot_tile - 1) QMLA_TR(4);
+            cp_async_mbar_arrive(bar(b_rfull + tb));
+          }
+        }
+        ok = !named_bar_or(kBarK, kKThreads - 32, !ok);
+      }
+    }
+    if (!ok) asm volatile("cp.async.wait_all;" ::: "memory");
+  } else if (warp >= kWarpK && warp < kWarpK + kNumKWarps) {
+    // ====================================================== K loads by cp.async (+ rms tail)
+    const int pt = threadIdx.x - kWarpK * 32;  // 0..95
+    const uint64_t pol_lat = policy_evict_normal();  // latent columns: read again for PV
+    const uint64_t pol_rope = policy_evict_first();  // rope columns: read once
+    const int ku = pt % kUnitsPerRow;                // this thread's 16-byte column unit
+    const int kt0 = pt / kUnitsPerRow;               // and first token
+    const int ksc = ku >> 3, kv = ku & 7;
+    SegCursor cur{row0, range_lo, range_hi};
+    int row, k0, k1, plo, phi;
+    uint32_t jt = 0;
+    Ring r;
+    bool ok = true;
+    while (ok && next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi)) {
+      int L = __ldg(a.seq_lens + row);
+      L = L < 0 ? 0 : L;
+      const int32_t* bt = a.block_table + (int64_t)row * a.bt_stride;
+      uint64_t nptr = pt < 64 ? token_row_addr(a, bt, L, k0, pt) : 0ull;
+      // L2 prefetch runs kPrefetchTiles ahead of the loads, so the DRAM requests
+      // in flight are not bounded by the shared-memory ring
+      if (pt < 64) {
+        for (int kp = k0; kp < min(k1, k0 + kPrefetchTiles); ++kp) {
+          const uint64_t pa = kp == k0 ? nptr : token_row_addr(a, bt, L, kp, pt);
+          if (pa) bulk_prefetch_l2(reinterpret_cast<const void*>(pa), a.pf_bytes, pol_lat);
+        }
+      }
+      for (int k = k0; k < k1 && ok; ++k, ++jt) {
+        const uint32_t tb = jt & 1;
+        if (pt < 64) tokptr[tb * 64 + pt] = nptr;
+        named_bar_sync(kBarK, kKThreads);
+        if (pt < 64 && k + kPrefetchTiles < k1) {
+          const uint64_t pa = token_row_addr(a, bt, L, k + kPrefetchTiles, pt);
+          if (pa) bulk_prefetch_l2(reinterpret_cast<const void*>(pa), a.pf_bytes, pol_lat);
+        }
+        if (pt < 64 && k + 1 < k1) nptr = token_row_addr(a, bt, L, k + 1, pt);  // next tile
+        const uint64_t* tp = tokptr + tb * 64;
+        // ---- rms tail of the tile -> staging buffer tb
+        if (a.rms_units > 0) {
+          if (jt >= 2) ok = mbar_wait(bar(b_rempty + tb), ((jt - 2) >> 1) & 1, abort_flag, status);
+          if (ok) {
+            for (int q = pt; q < kTile * a.rms_units; q += kKThreads) {
+              const int t = q / a.rms_units, u = q - t * a.rms_units;
+              const uint64_t src = tp[t];
+              const int col = a.rms_base_b + 16 * u;
+              const int nbytes = src ? max(0, min(16, a.row_bytes - col)) : 0;
+              cp_async_16_hint(rmsbuf + tb * (kTile * kRmsStride) + t * kRmsStride + 16 * u,
+                               nbytes ? reinterpret_cast<const void*>(src + col) : a.cache,
+                               (uint32_t)nbytes, pol_rope);
+            }
+            cp_async_mbar_arrive(bar(b_rfull + tb));
+          }
+        }
+        // ---- QK columns, one 128-dim slot at a time
+        for (int s = 0; s < a.n_qk_slots; ++s) {
+          if (ok) ok = mbar_wait(bar(b_kempty + r.idx), r.ph ^ 1, abort_flag, status);
+          if (pt == 0) QMLA_TRS(4, s);
+          if (pt == 0 && s == 0) QMLA_TR(0);
+          if (ok) {
+            const uint32_t dst0 = kring + r.idx * kSlotBytes + ksc * 8192;
+            const int colb = FP8 ? s * 128 + kv * 16 : (s * 128 + ksc * 64 + kv * 8) * 2;
+            const int nbytes = max(0, min(16, a.qk_bytes - colb));  // zero past the QK width
+            const uint64_t pol = s < NB ? pol_lat : pol_rope;
+#pragma unroll 4
+            for (int i = 0; i < kKIters; ++i) {
+              const int t = kt0 + i * kKTokStep;
+              if (t < kTile) {
+                const uint64_t src = tp[t];
+                const uint32_t nb = src ? (uint32_t)nbytes : 0u;
+                cp_async_16_hint(dst0 + t * 128 + ((kv ^ (t & 7)) << 4),
+                                 nb ? reinterpret_cast<const void*>(src + colb) : a.cache, nb, pol);
+              }
+            }
+            cp_async_mbar_arrive(bar(b_kfull + r.idx));
+          }
+          if (pt == 0) QMLA_TRS(1, s);
+          if (pt == 0 && s == a.n_qk_slots - 1) QMLA_TR(1);
+          r.next(nk);
+        }
+        // every K thread leaves the tile together (and tokptr[tb] is free again)
+        ok = !named_bar_or(kBarK, kKThreads, !ok);
+      }
+    }
+    if (!ok) asm volatile("cp.async.wait_all;" ::: "memory");
+  } else if (warp == kWarpV) {
+    // ====================================================== V loads by cp.async (from L2)
+    const uint64_t pol = policy_evict_first();
+    SegCursor cur{row0, range_lo, range_hi};
+    int row, k0, k1, plo, phi;
+    uint32_t jt = 0;
+    Ring r;
+    bool ok = true;
+    while (ok && next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi)) {
+      int L = __ldg(a.seq_lens + row);
+      L = L < 0 ? 0 : L;
+      const int32_t* bt = a.block_table + (int64_t)row * a.bt_stride;
+      for (int k = k0; k < k1 && ok; ++k, ++jt) {
+        const uint64_t p0 = token_row_addr(a, bt, L, k, lane);  // this lane's two tokens
+        const uint64_t p1 = token_row_addr(a, bt, L, k, lane + 32);
+        // the latent part is read again only after QK(jt) consumed it (it is in L2)
+        ok = mbar_wait(bar(b_kdone + (jt % kKdoneDepth)), (jt / kKdoneDepth) & 1, abort_flag,
+                       status);
+        ok = __all_sync(0xffffffffu, ok);
+        if (lane == 0) QMLA_TR(6);
+        for (int b = 0; b < NB && ok; ++b) {
+          ok = mbar_wait(bar(b_vempty + r.idx), r.ph ^ 1, abort_flag, status);
+          ok = __all_sync(0xffffffffu, ok);
+          if (ok) {
+            const uint32_t dst0 = vring + r.idx * kSlotBytes;
+            if constexpr (!FP8) {
+              // 64 tokens x 16 units: two tokens per warp step
+              const int u = lane & 15, sc = u >> 3, v = u & 7;
+              const int colb = (b * 128 + sc * 64 + v * 8) * 2;
+#pragma unroll 8
+              for (int i = 0; i < 32; ++i) {
+                const int t = 2 * i + (lane >> 4);
+                const uint64_t src = __shfl_sync(0xffffffffu, i < 16 ? p0 : p1, t & 31);
+                cp_async_16_hint(dst0 + sc * 8192 + t * 128 + ((v ^ (t & 7)) << 4),
+                                 src ? reinterpret_cast<const void*>(src + colb) : a.cache,
+                                 src ? 16u : 0u, pol);
+              }
+            } else {
+              // 64 tokens x 8 units: four tokens per warp step
+              const int v = lane & 7;
+              const int colb = b * 128 + v * 16;
+#pragma unroll 8
+              for (int i = 0; i < 16; ++i) {
+                const int t = 4 * i + (lane >> 3);
+                const uint64_t src = __shfl_sync(0xffffffffu, i < 8 ? p0 : p1, t & 31);
+                cp_async_16_hint(dst0 + t * 128 + ((v ^ (t & 7)) << 4),
+                                 src ? reinterpret_cast<const void*>(src + colb) : a.cache,
+                                 src ? 16u : 0u, pol);
+              }
+            }
+            cp_async_mbar_arrive(bar(b_vfull + r.idx));
+          }
+          if (lane == 0) QMLA_TRS(3, b);
+          r.next(nv);
+        }
+        if (lane == 0) QMLA_TR(13);
+      }
+    }
+    if (!ok) asm volatile("cp.async.wait_all;" ::: "memory");
+  } else if (warp == kWarpQK || warp == kWarpQK + 1) {
+    // ====================================================== QK issuers
+    // Each warp issues every other 16/32-wide K step of every sub-chunk into its
+    // own S partial (the softmax sums the partials): one thread issuing all
+    // MMAs of a tile is slower than the HBM stream.
+    const int qw = warp - kWarpQK;
+    if (lane == 0) {
+      const uint32_t idesc = FP8 ? make_idesc_f16(0, 64, 2 * NQK, 0, 0)
+                                 : make_idesc_f16(1, 64, NQK, 0, 0);
+      const uint32_t qc16 = a.q_chunk_bytes >> 4;              // Q chunk stride, descriptor units
+      const uint64_t q_desc0 = make_sdesc(qbuf, 16, 1024, 2);  // Q chunk 0 (K-major, 128B swizzle)
+      SegCursor cur{row0, range_lo, range_hi};
+      int row, k0, k1, plo, phi;
+      uint32_t jt = 0, sidx = 0;
+      Ring r;
+      bool ok = true;
+      while (ok && next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi)) {
+        ok = mbar_wait(bar(b_qfull), sidx & 1, abort_flag, status);
+        for (int k = k0; k < k1 && ok; ++k, ++jt) {
+          const uint32_t sb = jt % SB;
+          if (jt >= SB) ok = mbar_wait(bar(b_sempty + sb), ((jt - SB) / SB) & 1, abort_flag, status);
+          if (qw == 0) QMLA_TR(2);
+          tc_fence_after();
+          const uint32_t d_s = tmem_base + col_s + sb * SW + qw * SWP;
+          for (int s = 0; s < a.n_qk_slots && ok; ++s) {
+            ok = mbar_wait(bar(b_kfull + r.idx), r.ph, abort_flag, status);
+            if (!ok) break;
+            if (qw == 0) QMLA_TRS(2, s);
+            if (qw == 0 && s == 0) QMLA_TR(3);
+            if (qw == 0 && s == a.n_qk_slots - 1) QMLA_TR(4);
+            fence_proxy_async_smem();  // cp.async writes -> tensor-core reads
             tc_fence_after();
-            const uint64_t ad0 = make_sdesc(ring + cidx * kSlotBytes, 16, 1024, 2);
+            const uint64_t ad0 = make_sdesc(kring + r.idx * kSlotBytes, 16, 1024, 2);
             const uint64_t bd0 = q_desc0 + (uint64_t)(s * kSubs) * qc16;
 #pragma unroll
             for (int sc = 0; sc < kSubs; ++sc) {
               if (s * kSubs + sc < a.n_sub_qk) {
 #pragma unroll
-                for (int ks = 0; ks < 4; ++ks) {
+                for (int kk = 0; kk < 2; ++kk) {
+                  const int ks = 2 * kk + qw;
                   const uint64_t ad = ad0 + (uint64_t)(sc * 512 + ks * 2);
                   const uint64_t bd = bd0 + (uint64_t)(sc * qc16 + ks * 2);
-                  const uint32_t d = d_s + (ks % KP) * SWP;
-                  const uint32_t acc = (first && ks < KP) ? 0u : 1u;
+                  const uint32_t acc = (s == 0 && sc == 0 && kk == 0) ? 0u : 1u;
                   if constexpr (FP8)
-                    tc_mma_f8_ss(d, ad, bd, idesc, acc);
+                    tc_mma_f8_ss(d_s, ad, bd, idesc, acc);
                   else
-                    tc_mma_f16_ss(d, ad, bd, idesc, acc);
+                    tc_mma_f16_ss(d_s, ad, bd, idesc, acc);
                 }
-                first = false;
               }
             }
-            // FP8: the rope slot is free once these MMAs finish (rms was staged by the fix-up)
-            if (FP8 && s >= NB) tc_commit(bar(b_empty + cidx));
+            if (qw == 0) QMLA_TRS(5, s);
+            tc_commit(bar(b_kempty + r.idx));  // slot free once these MMAs complete
+            r.next(nk);
           }
-          if (ok) tc_commit(bar(b_sfull + sb));
-          QMLA_TR(5);
-        } else {
-          for (int t = 0; t < a.n_slot_tile; ++t)
-            if (++ridx == nslot) {
-              ridx = 0;
-              rph ^= 1;
-            }
+          if (ok) {
+            tc_commit(bar(b_sfull + sb));
+            tc_commit(bar(b_kdone + (jt % kKdoneDepth)));
+          }
+          if (qw == 0) QMLA_TR(5);
         }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
+        ++sidx;
       }
-      ++sidx;
+      if (jt > 0) {  // drain before TMEM is released
+        const uint32_t fb = bar(b_fin + qw);
+        tc_commit(fb);
+        volatile int never = 0;
+        mbar_wait(fb, 0, &never, nullptr, 100000000ull);
+      }
     }
-    if (lane == 0 && jt > 0) {  // drain before TMEM is released
-      tc_commit(bar(b_fin));
-      volatile int never = 0;
-      mbar_wait(bar(b_fin), 0, &never, nullptr, 100000000ull);
-    }
-  } else if (warp == kWarpPV) {
-    // ====================================================== PV issuer
-    const uint32_t idesc = FP8 ? make_idesc_f16(0, 128, 2 * NPV, 1, 1)
-                               : make_idesc_f16(1, 128, NPV, 1, 1);
-    SegCursor cur{row0, range_lo, range_hi};
-    int row, k0, k1, plo, phi;
-    uint32_t jt = 0, sidx = 0, tbase = 0;  // tbase: ring index of the tile's first slot
-    bool ok = true;
-    while (ok && next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi)) {
-      for (int k = k0; k < k1 && ok; ++k, ++jt) {
-        const uint32_t pb = jt & 1;  // P buffer / odone / rdone parity
-        if (lane == 0) {
-          if constexpr (!FP8) {
-            // bf16: rope slots (which hold the rms tail) are free once the softmax
-            // has read S and the rms values of this tile
-            ok = mbar_wait(bar(b_rdone + pb), (jt >> 1) & 1, abort_flag, status);
-            QMLA_TR(6);
-            if (ok)
-              for (int t = 0; t < nrope; ++t) {
-                uint32_t idx = tbase + t;
-                if (idx >= nslot) idx -= nslot;
-                mbar_arrive(bar(b_empty + idx));
-              }
-          }
-          if (ok) ok = mbar_wait(bar(b_pfull + pb), (jt >> 1) & 1, abort_flag, status);
-          QMLA_TR(7);
+    __syncwarp();
+  } else if (warp == kWarpPV || warp == kWarpPV + 1) {
+    // ====================================================== PV issuers
+    // Two warps, each owning about half of the 128-dim output blocks.
+    const int pw = warp - kWarpPV;
+    if (lane == 0) {
+      constexpr int NB0 = (NB + 1) / 2;
+      const int blk_lo = pw == 0 ? 0 : NB0, blk_hi = pw == 0 ? NB0 : NB;
+      const uint32_t idesc = FP8 ? make_idesc_f16(0, 128, NPV, 1, 1)
+                                 : make_idesc_f16(1, 128, NPV, 1, 1);
+      SegCursor cur{row0, range_lo, range_hi};
+      int row, k0, k1, plo, phi;
+      uint32_t jt = 0, sidx = 0;
+      Ring r;  // V ring position of block 0 of the current tile
+      bool ok = true;
+      while (ok && next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi)) {
+        for (int k = k0; k < k1 && ok; ++k, ++jt) {
+          const uint32_t pb = jt & 1;
+          ok = mbar_wait(bar(b_pfull + pb), (jt >> 1) & 1, abort_flag, status);
+          if (pw == 0) QMLA_TR(7);
           if (ok && k == k0 && sidx > 0)
             ok = mbar_wait(bar(b_ofree), (sidx - 1) & 1, abort_flag, status);
-          if (ok) {
+          // B = P^T (K = tokens, N = heads), MN-major, no swizzle: core matrix =
+          //   8 tokens x 16 bytes; LBO = token-group stride, SBO = head-block stride
+          const uint64_t bd0 = make_sdesc(pbuf + pb * a.p_bytes, 16 * NPV, 128, 0);
+          Ring rv = r;
+          for (int b = 0; b < NB; ++b) {
+            const uint32_t vidx = rv.idx, vph = rv.ph;
+            rv.next(nv);
+            if (!ok || b < blk_lo || b >= blk_hi) continue;
+            ok = mbar_wait(bar(b_vfull + vidx), vph, abort_flag, status);
+            if (!ok) continue;
+            QMLA_TRS(3, 8 + b);
+            fence_proxy_async_smem();  // cp.async-written V slot -> tensor-core reads
             tc_fence_after();
-            // B = P^T (K = tokens, N = heads), MN-major, no swizzle: core matrix =
-            //   8 tokens x 16 bytes; SBO = head-block stride, LBO = token-group stride
-            const uint64_t bd0 = make_sdesc(pbuf + pb * a.p_bytes, 16 * NPV, 128, 0);
             // A = V^T (M = 128 dims, K = tokens), MN-major, 128-byte swizzle:
             //   LBO = stride between 64-dim halves (bf16), SBO = 8-token group stride
-            uint64_t ad0[NB];
-            uint32_t vidx[NB];
-#pragma unroll
-            for (int blk = 0; blk < NB; ++blk) {
-              uint32_t idx = tbase + nrope + blk;
-              if (idx >= nslot) idx -= nslot;
-              vidx[blk] = idx;
-              ad0[blk] = make_sdesc(ring + idx * kSlotBytes, 8192, 1024, 2);
-            }
+            const uint64_t ad0 = make_sdesc(vring + vidx * kSlotBytes, 8192, 1024, 2);
+            const uint32_t d_o = tmem_base + col_o + b * OW;
 #pragma unroll
             for (int ks = 0; ks < kPvSteps; ++ks) {
-              // blocks inner: consecutive MMAs go to different accumulators
-#pragma unroll
-              for (int blk = 0; blk < NB; ++blk) {
-                const uint32_t d_o = tmem_base + col_o + blk * OW;
-                const uint64_t ad = ad0[blk] + (uint64_t)(ks * (kPvAStep >> 4));
-                const uint64_t bd = bd0 + (uint64_t)(ks * (kPvBStep >> 4));
-                const uint32_t acc = (k == k0 && ks == 0) ? 0u : 1u;
-                if constexpr (FP8)
-                  tc_mma_f8_ss(d_o, ad, bd, idesc, acc);
-                else
-                  tc_mma_f16_ss(d_o, ad, bd, idesc, acc);
+              const uint64_t ad = ad0 + (uint64_t)(ks * (kPvAStep >> 4));
+              const uint64_t bd = bd0 + (uint64_t)(ks * (kPvBStep >> 4));
+              const uint32_t acc = (k == k0 && ks == 0) ? 0u : 1u;
+              if constexpr (FP8) {
+                // P = P_hi + P_lo: the lo half starts NPV/16 head blocks further on
+                tc_mma_f8_ss(d_o, ad, bd, idesc, acc);
+                tc_mma_f8_ss(d_o, ad, bd + (uint64_t)((8 * NPV) >> 4), idesc, 1u);
+              } else {
+                tc_mma_f16_ss(d_o, ad, bd, idesc, acc);
               }
             }
-#pragma unroll
-            for (int blk = 0; blk < NB; ++blk) tc_commit(bar(b_empty + vidx[blk]));
-            tc_commit(bar(b_odone + pb));
-            QMLA_TR(8);
+            tc_commit(bar(b_vempty + vidx));
           }
+          r = rv;
+          if (ok) tc_commit(bar(b_odone + pb));
+          if (pw == 0) QMLA_TR(8);
         }
-        tbase += a.n_slot_tile;
-        if (tbase >= nslot) tbase -= nslot;
-        ok = __shfl_sync(0xffffffffu, ok, 0);
+        ++sidx;
       }
-      ++sidx;
-    }
-    if (lane == 0 && jt > 0) {
-      tc_commit(bar(b_fin + 1));
-      volatile int never = 0;
-      mbar_wait(bar(b_fin + 1), 0, &never, nullptr, 100000000ull);
-    }
-  } else if (FP8 && warp == kWarpFix) {
-    // ====================================================== FP8 rms fix-up
-    uint8_t* rmsbuf = smem + a.off_rms;
-    const int qk = a.qk_dim;
-    const int zero_end = a.n_qk_slots * 128;  // MMA K boundary (bytes)
-    SegCursor cur{row0, range_lo, range_hi};
-    int row, k0, k1, plo, phi;
-    uint32_t jt = 0;
-    bool ok = true;
-    while (ok && a.fix_slot0 >= 0 && next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi)) {
-      for (int k = k0; k < k1 && ok; ++k, ++jt) {
-        const uint32_t rb = jt & 1;
-        if (lane == 0 && jt >= 2)
-          ok = mbar_wait(bar(b_rempty + rb), ((jt - 2) >> 1) & 1, abort_flag, status);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        for (int s = a.fix_slot0; s < a.n_slot_tile && ok; ++s) {
-          uint32_t it = jt * a.n_slot_tile + pos_of(s);
-          if (lane == 0) ok = mbar_wait(bar(b_full + it % nslot), (it / nslot) & 1, abort_flag, status);
-          ok = __shfl_sync(0xffffffffu, ok, 0);
-          if (!ok) break;
-          uint8_t* sl = smem + a.off_ring + (it % nslot) * kSlotBytes;
-          const int s0 = s * 128;
-          // rms bytes of this slot -> staging[row][b - rms_offset]
-          const int lo = max(a.rms_offset, s0), hi = min(a.rms_offset + a.rms_bytes, s0 + 128);
-          for (int r = lane; r < kTile; r += 32) {
-            for (int b = lo; b < hi; ++b) {
-              int off = b - s0;
-              rmsbuf[rb * (kTile * 64) + r * 64 + (b - a.rms_offset)] =
-                  sl[r * 128 + ((((off >> 4) ^ (r & 7))) << 4) + (off & 15)];
-            }
-          }
-          __syncwarp();
-          // bytes in [qk, zero_end) of this slot would meet the MMA: zero them
-          const int zlo = max(qk, s0), zhi = min(zero_end, s0 + 128);
-          for (int r = lane; r < kTile; r += 32)
-            for (int b = zlo; b < zhi; ++b) {
-              int off = b - s0;
-              sl[r * 128 + ((((off >> 4) ^ (r & 7))) << 4) + (off & 15)] = 0;
-            }
-          if (s >= a.n_qk_slots) {  // rms-only slot: nothing else reads it
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(b_empty + it % nslot));
-          }
-        }
-        if (!ok) break;
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(b_fix + rb));
+      if (jt > 0) {
+        const uint32_t fb = bar(b_fin + 2 + pw);
+        tc_commit(fb);
+        volatile int never = 0;
+        mbar_wait(fb, 0, &never, nullptr, 100000000ull);
       }
     }
+    __syncwarp();
   } else if (warp < kSoftmaxWarps) {
     // ====================================================== softmax / epilogue
+    // Every wait result is folded into a barrier the whole group takes, so the
+    // 256 threads always leave a tile (or the kernel) together.
     const int tid = threadIdx.x;  // 0..255
     const int sp = warp & 3;      // TMEM sub-partition
     const int hw = warp >> 2;     // head half
@@ -598,12 +747,12 @@ __global__ void __launch_bounds__(FP8 ? 384 : 352, 1)
     };
     const float kscale = (FP8 && a.k_scale) ? __ldg(a.k_scale) : 1.0f;
     const bool cap = a.logit_cap > 0.f;
+    const uint8_t* rms_smem = smem + a.off_rms;
     float m_ref[NJ], l_part[NJ], gs[NJ];
     SegCursor cur{row0, range_lo, range_hi};
     int row, k0, k1, plo, phi;
     uint32_t jt = 0, sidx = 0;
     bool ok = true;
-    const uint8_t* rmsbuf = smem + a.off_rms;
     while (ok && next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi)) {
       int L = __ldg(a.seq_lens + row);
       L = L < 0 ? 0 : L;
@@ -620,7 +769,10 @@ __global__ void __launch_bounds__(FP8 ? 384 : 352, 1)
                                                  (d0 - a.rank)) * 2;
             if ((lat ? a.q_vec : a.qpe_vec) && d0 + 8 <= a.qk_dim && a.q_dtype == 0) {
               uint4 v = __ldg(reinterpret_cast<const uint4*>(src));
-              w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+              w[0] = v.x;
+              w[1] = v.y;
+              w[2] = v.z;
+              w[3] = v.w;
             } else {
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
@@ -639,9 +791,10 @@ __global__ void __launch_bounds__(FP8 ? 384 : 352, 1)
         for (int h = warp; h < H; h += kSoftmaxWarps) {
           float mx = 0.f;
           for (int d = lane; d < a.qk_dim; d += 32) {
-            const uint8_t* src = d < a.rank
-                ? a.q + ((int64_t)row * a.q_sr + (int64_t)h * a.q_sh + d) * 2
-                : a.q_pe + ((int64_t)row * a.qpe_sr + (int64_t)h * a.qpe_sh + (d - a.rank)) * 2;
+            const uint8_t* src =
+                d < a.rank
+                    ? a.q + ((int64_t)row * a.q_sr + (int64_t)h * a.q_sh + d) * 2
+                    : a.q_pe + ((int64_t)row * a.qpe_sr + (int64_t)h * a.qpe_sh + (d - a.rank)) * 2;
             mx = fmaxf(mx, fabsf(load_as_float(src, a.q_dtype)));
           }
 #pragma unroll
@@ -662,9 +815,10 @@ __global__ void __launch_bounds__(FP8 ? 384 : 352, 1)
               const int d = d0 + e;
               uint8_t b = 0;
               if (d < a.qk_dim) {
-                const uint8_t* src = d < a.rank
-                    ? a.q + ((int64_t)row * a.q_sr + (int64_t)h * a.q_sh + d) * 2
-                    : a.q_pe + ((int64_t)row * a.qpe_sr + (int64_t)h * a.qpe_sh + (d - a.rank)) * 2;
+                const uint8_t* src =
+                    d < a.rank ? a.q + ((int64_t)row * a.q_sr + (int64_t)h * a.q_sh + d) * 2
+                               : a.q_pe + ((int64_t)row * a.qpe_sr + (int64_t)h * a.qpe_sh +
+                                           (d - a.rank)) * 2;
                 const float x = load_as_float(src, a.q_dtype) * sc;
                 const uint8_t hi = f32_to_e4m3(x);
                 b = lo_row ? f32_to_e4m3(x - e4m3_to_f32(hi)) : hi;
@@ -688,18 +842,18 @@ __global__ void __launch_bounds__(FP8 ? 384 : 352, 1)
       }
 
       // ---------------- tiles
-      for (int k = k0; k < k1 && ok; ++k, ++jt) {
-        const uint32_t sb = jt % SB;   // S buffer
-        const uint32_t pb = jt & 1;    // P buffer / odone / rdone parity
+      for (int k = k0; k < k1; ++k, ++jt) {
+        const uint32_t sb = jt % SB;  // S buffer
+        const uint32_t pb = jt & 1;   // P buffer / odone / rms parity
         const int nvalid = min(kTile, L - k * kTile);
         const bool valid = tt < nvalid;
-        const uint32_t tbase = (jt * a.n_slot_tile) % nslot;  // ring index of this tile's first slot
         float x[NJ];
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) x[j] = 0.f;
         ok = mbar_wait(bar(b_sfull + sb), (jt / SB) & 1, abort_flag, status);
-        if (!ok) break;
         if (tid == 0) QMLA_TR(9);
-        tc_fence_after();
-        {
+        if (ok) {
+          tc_fence_after();
           const uint32_t tb = tmem_base + lane_base + col_s + sb * SW + hw * (nqk >> 1);
           // S = sum of the KP partials (and of the hi / lo halves for FP8)
           float xp[KP * (FP8 ? 2 : 1)][NJ];
@@ -716,75 +870,50 @@ __global__ void __launch_bounds__(FP8 ? 384 : 352, 1)
             for (int p = 0; p < KP * (FP8 ? 2 : 1); ++p) v += xp[p][j];
             x[j] = v;
           }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(b_sempty + sb));
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(b_sempty + sb));
         // ---- rms divisor -> per-(token, head) factor
         float f[NJ];
 #pragma unroll
         for (int j = 0; j < NJ; ++j) f[j] = gs[j];
-        if (a.rms_mode != 0) {
-          if constexpr (!FP8) {
+        if (a.rms_units > 0 && ok) {
+          ok = mbar_wait(bar(b_rfull + pb), (jt >> 1) & 1, abort_flag, status);
+          if (ok) {
             if (valid) {
+              const uint8_t* rp = rms_smem + pb * (kTile * kRmsStride) + tt * kRmsStride + a.rms_skip;
 #pragma unroll
               for (int j = 0; j < NJ; ++j) {
-                if (j < nj && head[j] < H) {
-                  const int d = a.rms_offset + head[j];
-                  const int s = d >> 7, e = d & 127;
-                  const uint32_t sl = slot_at(tbase, pos_of(s)) + (e >> 6) * 8192;
-                  uint16_t bits;
-                  asm volatile("ld.shared.u16 %0, [%1];"
-                               : "=h"(bits)
-                               : "r"(sw128(sl, tt, (e & 63) >> 3) + (e & 7) * 2));
-                  const float r = __bfloat162float(__ushort_as_bfloat16(bits));
-                  f[j] = r > 0.f ? __fdividef(gs[j], r) : gs[j];
-                }
-              }
-            }
-          } else {
-            ok = mbar_wait(bar(b_fix + pb), (jt >> 1) & 1, abort_flag, status);
-            if (!ok) break;
-            if (valid) {
-              const uint8_t* rp = rmsbuf + pb * (kTile * 64) + tt * 64;
-#pragma unroll
-              for (int j = 0; j < NJ; ++j) {
-                if (j < nj && head[j] < H) {
+                if (head[j] < H) {
                   const int h = head[j];
-                  if (a.rms_mode == 3) {
+                  if (FP8 && a.rms_mode == 3) {
                     // 1 / rms = 2^(3 - code * 6/255)
                     f[j] = gs[j] * exp2f(3.0f - (float)rp[h] * (6.0f / 255.0f));
                   } else {
-                    float r;
-                    if (a.rms_mode == 2)
-                      r = __bfloat162float(__ushort_as_bfloat16(
+                    float rv;
+                    if (!FP8 || a.rms_mode == 2)
+                      rv = __bfloat162float(__ushort_as_bfloat16(
                           (uint16_t)rp[2 * h] | ((uint16_t)rp[2 * h + 1] << 8)));
                     else
-                      r = e4m3_to_f32(rp[h]) * kscale;
-                    f[j] = r > 0.f ? __fdividef(gs[j], r) : gs[j];
+                      rv = e4m3_to_f32(rp[h]) * kscale;
+                    f[j] = rv > 0.f ? __fdividef(gs[j], rv) : gs[j];
                   }
                 }
               }
             }
-          }
-        }
-        if constexpr (FP8) {
-          // the fix-up may stage the next-but-one tile only after this one is consumed
-          if (a.fix_slot0 >= 0) {
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(b_rempty + pb));
           }
         }
-        // PV(jt-2) must be done before P buffer sb is rewritten; waiting here also
-        // keeps the rms-released signal below at most one phase ahead of its reader
-        if (jt >= 2) {
+        // PV(jt-2) must be done before P buffer pb is rewritten
+        if (jt >= 2 && ok) {
           const uint32_t jp = jt - 2;
           ok = mbar_wait(bar(b_odone + (jp & 1)), (jp >> 1) & 1, abort_flag, status);
-          if (!ok) break;
         }
-        if constexpr (!FP8) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(b_rdone + pb));
+        if (named_bar_or(kBarSoftmax, kSoftmaxThreads, !ok)) {
+          ok = false;
+          break;
         }
         if (tid == 0) QMLA_TR(10);
         // ---- logits (log2 units) and the lazy-rescale test
@@ -792,7 +921,7 @@ __global__ void __launch_bounds__(FP8 ? 384 : 352, 1)
 #pragma unroll
         for (int j = 0; j < NJ; ++j) {
           float v = -INFINITY;
-          if (valid && j < nj && head[j] < H) {
+          if (valid && head[j] < H) {
             float s = x[j] * f[j];
             if (cap) s = a.logit_cap * tanhf(s / a.logit_cap);
             v = s * kLog2e;
@@ -827,7 +956,8 @@ __global__ void __launch_bounds__(FP8 ? 384 : 352, 1)
             float t = fmaxf(fmaxf(red[(hw * 4 + 0) * 32 + c2], red[(hw * 4 + 1) * 32 + c2]),
                             fmaxf(red[(hw * 4 + 2) * 32 + c2], red[(hw * 4 + 3) * 32 + c2]));
             float mn = fmaxf(m_ref[j], t);
-            float al = (mn == -INFINITY) ? 1.f : (m_ref[j] == -INFINITY ? 0.f : exp2f(m_ref[j] - mn));
+            float al = (mn == -INFINITY) ? 1.f
+                                         : (m_ref[j] == -INFINITY ? 0.f : exp2f(m_ref[j] - mn));
             alpha[j] = al;
             any_scale |= (al != 1.f) && (k > k0);
             m_ref[j] = mn;
@@ -838,24 +968,21 @@ __global__ void __launch_bounds__(FP8 ? 384 : 352, 1)
             // O holds tiles k0..k-1: wait for PV(k-1), then rescale it in TMEM
             if (sp == 0 && lane < 4 && (lane & 1) == 0) {
 #pragma unroll
-              for (int j = 0; j < NJ; ++j)
-                if (j < nj) hv[head[j] & 31] = alpha[j];
+              for (int j = 0; j < NJ; ++j) hv[head[j] & 31] = alpha[j];
             }
             named_bar_sync(kBarSoftmax, kSoftmaxThreads);
             const uint32_t jp = jt - 1;
             ok = mbar_wait(bar(b_odone + (jp & 1)), (jp >> 1) & 1, abort_flag, status);
-            if (!ok) break;
-            tc_fence_after();
-            float an[NPV / 2];
+            if (ok) {
+              tc_fence_after();
+              float an[NPV / 2];
 #pragma unroll
-            for (int i = 0; i < NPV / 2; ++i) {
-              int h = head_of_n(hw * (NPV / 2) + i);
-              an[i] = h >= 0 ? hv[h] : 1.f;
-            }
-            for (int blk = 0; blk < NB; ++blk) {
-#pragma unroll
-              for (int part = 0; part < (FP8 ? 2 : 1); ++part) {
-                const uint32_t ta = tmem_base + lane_base + col_o + blk * OW + part * NPV + hw * (NPV / 2);
+              for (int i = 0; i < NPV / 2; ++i) {
+                int h = head_of_n(hw * (NPV / 2) + i);
+                an[i] = h >= 0 ? hv[h] : 1.f;
+              }
+              for (int blk = 0; blk < NB; ++blk) {
+                const uint32_t ta = tmem_base + lane_base + col_o + blk * OW + hw * (NPV / 2);
 #pragma unroll
                 for (int g8 = 0; g8 < NPV / 16; ++g8) {
                   float ov[8];
@@ -866,12 +993,15 @@ __global__ void __launch_bounds__(FP8 ? 384 : 352, 1)
                   tmem_st8(ta + g8 * 8, ov);
                 }
               }
+              tmem_wait_st();
             }
-            tmem_wait_st();
-            named_bar_sync(kBarSoftmax, kSoftmaxThreads);  // hv[] free again
+            if (named_bar_or(kBarSoftmax, kSoftmaxThreads, !ok)) {  // hv[] free again
+              ok = false;
+              break;
+            }
           }
         }
-        // ---- P = 2^(x - m) -> P^T buffer sb
+        // ---- P = 2^(x - m) -> P^T buffer pb
         {
           float p[NJP];
 #pragma unroll
@@ -921,16 +1051,6 @@ __global__ void __launch_bounds__(FP8 ? 384 : 352, 1)
               st_shared_u32(al, wlo[0]);
             }
           }
-          // tokens past the row end: zero their latent rows so P.V stays finite
-          if (!valid) {
-            constexpr int upr = kSlotBytes / kTile / 16;  // 16-byte units per token per slot
-            const int q4 = 2 * hw + cpar;
-            for (int i = q4; i < NB * upr; i += 4) {
-              const int blk = i / upr, u = i - blk * upr;
-              const uint32_t base = slot_at(tbase, nrope + blk) + (u >> 3) * 8192 + tt * 128 + (u & 7) * 16;
-              st_shared_v4(base, 0u, 0u, 0u, 0u);
-            }
-          }
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -943,8 +1063,6 @@ __global__ void __launch_bounds__(FP8 ? 384 : 352, 1)
       {
         const uint32_t jl = jt - 1;
         ok = mbar_wait(bar(b_odone + (jl & 1)), (jl >> 1) & 1, abort_flag, status);
-        if (!ok) break;
-        tc_fence_after();
         float ls[NJ];
 #pragma unroll
         for (int j = 0; j < NJ; ++j) {
@@ -959,12 +1077,16 @@ __global__ void __launch_bounds__(FP8 ? 384 : 352, 1)
 #pragma unroll
           for (int j = 0; j < NJ; ++j) red[(hw * 4 + sp) * 32 + 2 * j + cpar] = ls[j];
         }
-        named_bar_sync(kBarSoftmax, kSoftmaxThreads);
+        if (named_bar_or(kBarSoftmax, kSoftmaxThreads, !ok)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
         if (sp == 0 && lane < 4 && (lane & 1) == 0) {
 #pragma unroll
           for (int j = 0; j < NJ; ++j) {
             const int c2 = 2 * j + cpar;
-            if (j < nj && head[j] < H) {
+            if (head[j] < H) {
               float lt = red[(hw * 4 + 0) * 32 + c2] + red[(hw * 4 + 1) * 32 + c2] +
                          red[(hw * 4 + 2) * 32 + c2] + red[(hw * 4 + 3) * 32 + c2];
               hv[32 + head[j]] = lt;
@@ -988,29 +1110,11 @@ __global__ void __launch_bounds__(FP8 ? 384 : 352, 1)
           const int d = blk * 128 + sp * 32 + lane;
           const uint32_t ta = tmem_base + lane_base + col_o + blk * OW + hw * (NPV / 2);
           float ov[NPV / 2];
-          if constexpr (NPV == 32) {
+          if constexpr (NPV == 32)
             tmem_ld16(ta, ov);
-            if constexpr (FP8) {
-              float ol[16];
-              tmem_ld16(ta + NPV, ol);
-              tmem_wait_ld();
-#pragma unroll
-              for (int i = 0; i < 16; ++i) ov[i] += ol[i];
-            } else {
-              tmem_wait_ld();
-            }
-          } else {
+          else
             tmem_ld8(ta, ov);
-            if constexpr (FP8) {
-              float ol[8];
-              tmem_ld8(ta + NPV, ol);
-              tmem_wait_ld();
-#pragma unroll
-              for (int i = 0; i < 8; ++i) ov[i] += ol[i];
-            } else {
-              tmem_wait_ld();
-            }
-          }
+          tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < NPV / 2; ++i) {
             const int h = hn[i];
