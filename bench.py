@@ -1,0 +1,399 @@
+#!/usr/bin/env python3
+"""Benchmark of the sm_100a paged MLA decode: achieved HBM TB/s (and seqs/s) on BASELINE config 1.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the plugin's real row split): bf16 latent cache, batch 64,
+1 query token, 24 heads, context lengths U[1024, 32768] (torch generator seed 1), 16-token
+pages in random order, row = latent 768 | rope 232 | rms 24 (1024 bf16), q ~ N(0,1)/sqrt(1024),
+cache ~ N(0,1), rms ~ U(0.5, 2).  Synthetic, seeded; the 2.44 GB cache is larger than L2, so
+no L2 flush is needed between steps.
+
+One step = one decode call over the whole batch.  N = 1: qmla_mla_decode on one GPU.  N > 1
+(launched with torchrun, one process per GPU): decode context parallelism -- every rank holds a
+contiguous 1/N slice of every sequence's KV, decodes it, and the (o, lse) partials are merged
+over NCCL (all-gather of lse, the correction kernel, all-reduce of o) -- the total work is fixed
+("scaling": "strong").
+
+``--impl reference`` times the reference's algorithm on the host cores instead: the numpy
+restatement in oracle/ (the reference's own CPU path is torch code that cannot travel to the GPU
+box), on a bounded sample of the same workload; under torchrun only rank 0 runs.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import pathlib
+import statistics
+import sys
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MLA decode attn achieved HBM TB/s (% peak) and seqs/s at 1/2/4/8 B200"
+B, H, RANK, ROPE, PAGE = 64, 24, 768, 232, 16
+QK = RANK + ROPE  # attention width = rms offset
+ROW = 1024        # elements per cache row (768 | 232 | 24)
+ROW_READ = QK * 2 + H * 2  # bytes of a row the decode reads: latent + rope + rms tail
+WORKLOAD = ("config1: bf16 latent paged MLA decode, B=64, 1 query token, 24 heads, "
+            "row 768|232|24 bf16, L~U[1024,32768] (seed 1), 16-token pages in random order")
+
+
+def seq_lens_cfg1() -> list[int]:
+    import torch
+    return torch.randint(1024, 32769, (B,), generator=torch.Generator().manual_seed(1)).tolist()
+
+
+def algorithmic_bytes(lens: list[int], rows: int) -> int:
+    """Cache rows read once + page table + q + o + lse (the path's unavoidable traffic)."""
+    pages = sum((L + PAGE - 1) // PAGE for L in lens)
+    return (sum(lens) * ROW_READ + 4 * pages + rows * H * QK * 2 + rows * H * RANK * 2 + rows * H * 4)
+
+
+def measured_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except Exception:  # noqa: BLE001
+        return 6650.0, "fallback"
+
+
+def profile_traffic() -> float | None:
+    """DRAM bytes per decode launch from the committed ncu summary of this workload."""
+    p = ROOT / "profiles" / "decode_bf16_config1.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML (read-only) in a thread."""
+
+    NAMES = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+             0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+             0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, index: int, period_s: float = 0.005):
+        self.samples: list[tuple[float, int, int]] = []
+        self.period = period_s
+        self._stop = threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:  # noqa: BLE001
+            self.max_mhz = None
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((time.perf_counter(), mhz, reasons))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self.period)
+
+    def start(self):
+        if self.ok:
+            self._t.start()
+        return self
+
+    def stop(self):
+        self._stop.set()
+        if self.ok:
+            self._t.join(timeout=2)
+
+    def summary(self, t0: float, t1: float) -> dict:
+        win = [s for s in self.samples if t0 <= s[0] <= t1]
+        if not win and self.samples:  # timed region shorter than one period: nearest samples
+            win = sorted(self.samples, key=lambda s: min(abs(s[0] - t0), abs(s[0] - t1)))[:3]
+        if not win:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        bits = 0
+        for s in win:
+            bits |= s[2]
+        reasons = [n for b, n in self.NAMES.items() if bits & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(s[1] for s in win), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(win)}
+
+
+def make_inputs(lens: list[int], device, seed: int):
+    """Cache holding exactly the given sequences (pages shuffled), q, block table, lengths."""
+    import torch
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    pages = [(L + PAGE - 1) // PAGE for L in lens]
+    P = max(1, sum(pages))
+    gd = torch.Generator(device=device).manual_seed(seed)
+    cache = torch.randn(P, PAGE, 1, ROW, device=device, dtype=torch.bfloat16, generator=gd)
+    cache[..., QK:] = (torch.rand(P, PAGE, 1, ROW - QK, device=device, generator=gd) * 1.5 + 0.5).to(torch.bfloat16)
+    perm = torch.randperm(P, generator=g)
+    bt = torch.zeros(len(lens), max(1, max(pages)), dtype=torch.int32)
+    off = 0
+    for b, n in enumerate(pages):
+        bt[b, :n] = perm[off:off + n].to(torch.int32)
+        off += n
+    q = (torch.randn(len(lens), H, QK, generator=g) / math.sqrt(1024)).to(torch.bfloat16)
+    return cache, q, bt, torch.tensor(lens, dtype=torch.int32)
+
+
+# ------------------------------------------------------------------------------ CPU reference arm
+def cpu_reference_sample(lens: list[int], budget_s: float, seed: int = 1):
+    """Time the oracle (numpy restatement of the reference algorithm) on whole sequences of the
+    workload until ~budget_s of CPU time; returns (bytes, seconds, n_seqs, threads)."""
+    import numpy as np
+
+    import oracle
+    rng = np.random.default_rng(seed)
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max([i.get("num_threads", 1) for i in threadpool_info()] + [1])
+    except Exception:  # noqa: BLE001
+        threads = 1
+    done_bytes, spent, n = 0, 0.0, 0
+    for L in lens:
+        pps = (L + PAGE - 1) // PAGE
+        cache = oracle.f32_to_bf16_bits(rng.standard_normal((pps, PAGE, ROW), dtype=np.float32))
+        cache[..., QK:] = oracle.f32_to_bf16_bits(rng.uniform(0.5, 2.0, (pps, PAGE, ROW - QK)).astype(np.float32))
+        bt = rng.permutation(pps).reshape(1, pps).astype(np.int32)
+        q = oracle.bf16_round((rng.standard_normal((1, H, QK)) / 32).astype(np.float32))
+        t0 = time.perf_counter()
+        oracle.decode(q, cache, bt, np.array([L]), rank=RANK, qk_dim=QK, page_size=PAGE, sm_scale=1 / 16,
+                      rms_offset=QK)
+        spent += time.perf_counter() - t0
+        done_bytes += algorithmic_bytes([L], 1)
+        n += 1
+        if spent >= budget_s:
+            break
+    return done_bytes, spent, n, threads
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    lens = seq_lens_cfg1()
+    # one step = one sequence of the workload (bounded sample), cycling through the batch
+    times, nbytes = [], []
+    for i in range(args.warmup + args.steps):
+        b, s, _, threads = cpu_reference_sample([lens[i % B]], 0.0, seed=i)
+        if i >= args.warmup:
+            times.append(s)
+            nbytes.append(b)
+    tot_s, tot_b = sum(times), sum(nbytes)
+    value = tot_b / tot_s / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot_s / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded), host memory",
+        "config": {"workload": WORKLOAD, "sample": "one whole sequence of the batch per step"},
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} sequences of config1 (one per step), numpy oracle"},
+        "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------ GPU arm
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+
+    from qwen_mla_vllm_b200.dcp import correct_attn_out, lse_all_gather, shard_lengths
+    from qwen_mla_vllm_b200.mla_decode_attention import build_params, run_params
+
+    lens_all = seq_lens_cfg1()[:args.batch]
+    lens = shard_lengths(lens_all, world, rank) if world > 1 else lens_all
+    cache, q_h, bt_h, sl_h = make_inputs(lens, dev, seed=1000 + rank)
+    q, bt, sl = q_h.to(dev), bt_h.to(dev), sl_h.to(dev)
+    o_dtype = torch.float32 if world > 1 else torch.bfloat16
+    nb = len(lens_all)
+    o = torch.empty(nb, H, RANK, dtype=o_dtype, device=dev)
+    lse = torch.empty(nb, H, dtype=torch.float32, device=dev)
+    params = build_params(q, cache, o, lse, bt, sl, rank=RANK, qk_dim=QK, rms_offset=QK, rms_mode=1,
+                          page_size=PAGE, sm_scale=1 / 16)
+    run_params(params, dev)  # sizes and attaches the workspace once
+    stream = torch.cuda.current_stream(dev)
+    launches_per_step = 3  # plan, decode, split merge
+
+    def step():
+        run_params(params, dev)
+        if world > 1:
+            lses = lse_all_gather(lse)
+            correct_attn_out(o, lses, rank)
+            dist.all_reduce(o)
+
+    # clock ramp: ~1 s of untimed decode so the SM clock leaves its idle state, then W warm-up steps
+    t_end = time.perf_counter() + 1.0
+    while time.perf_counter() < t_end:
+        for _ in range(5):
+            step()
+        torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        step()
+    sampler = ClockSampler(local).start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        run_params(params, dev)
+        ev[i][1].record(stream)
+        if world > 1:
+            lses = lse_all_gather(lse)
+            correct_attn_out(o, lses, rank)
+            dist.all_reduce(o)
+    stop.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t1 = time.perf_counter()
+    sampler.stop()
+    ms = start.elapsed_time(stop)
+    decode_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    mine = algorithmic_bytes(lens, nb)
+    if world > 1:
+        t = torch.tensor([ms, float(mine), decode_ms], dtype=torch.float64, device=dev)
+        tmax = t.clone()
+        dist.all_reduce(tmax[:1], op=dist.ReduceOp.MAX)
+        tsum = t.clone()
+        dist.all_reduce(tsum[1:2], op=dist.ReduceOp.SUM)
+        ms, total_bytes = float(tmax[0]), float(tsum[1])
+    else:
+        total_bytes = float(mine)
+    step_ms = ms / args.steps
+    value = total_bytes / (step_ms * 1e-3) / 1e12
+    peak, peak_kind = measured_peak()
+    achieved_gbs = mine / (decode_ms * 1e-3) / 1e9
+    traffic = profile_traffic() if world == 1 else None
+    clocks = sampler.summary(t0, t1)
+
+    # ---- end to end through the public entry point with host buffers (pinned) every step
+    from qwen_mla_vllm_b200.mla_decode_attention import decode_attention_fwd
+    q_pin, bt_pin, sl_pin = q_h.pin_memory(), bt_h.pin_memory(), sl_h.pin_memory()
+    o_host = torch.empty(nb, H, RANK, dtype=o_dtype).pin_memory()
+    lse_host = torch.empty(nb, H, dtype=torch.float32).pin_memory()
+    logits = torch.empty(nb, H, 8, RANK + 1, dtype=torch.float32, device=dev)
+    q_d, bt_d, sl_d = torch.empty_like(q), torch.empty_like(bt), torch.empty_like(sl)
+
+    def e2e_step():
+        q_d.copy_(q_pin, non_blocking=True)
+        bt_d.copy_(bt_pin, non_blocking=True)
+        sl_d.copy_(sl_pin, non_blocking=True)
+        decode_attention_fwd(q_d, cache, cache[..., :RANK], o, lse, bt_d, sl_d, logits, 8, 1 / 16, PAGE,
+                             is_mla=True, rms_offset=QK)
+        if world > 1:
+            lses = lse_all_gather(lse)
+            correct_attn_out(o, lses, rank)
+            dist.all_reduce(o)
+        o_host.copy_(o, non_blocking=True)
+        lse_host.copy_(lse, non_blocking=True)
+
+    for _ in range(max(3, args.warmup)):
+        e2e_step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t[0])
+    e2e_value = total_bytes / (e2e_ms / args.steps * 1e-3) / 1e12
+    h2d = (q.numel() * q.element_size() + bt.numel() * 4 + sl.numel() * 4) * world
+    d2h = (o.numel() * o.element_size() + lse.numel() * 4) * world
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb, cs, n, threads = cpu_reference_sample(lens_all, args.cpu_budget)
+        cpu = {"value": cb / cs / 1e12, "unit": "TB/s", "cores": threads, "kind": "port",
+               "sample": f"{n} of the {nb} sequences ({cb / 1e9:.2f} GB of rows), numpy oracle, {cs:.1f} s"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded), random-init cache in the plugin's row layout",
+            "config": {"workload": WORKLOAD if nb == B else f"{WORKLOAD} -- first {nb} sequences only",
+                       "batch": nb, "heads": H, "rank": RANK, "rope": ROPE,
+                       "rms": H, "row_bytes_read": ROW_READ, "page_size": PAGE, "sum_context": sum(lens_all),
+                       "parallelism": f"dcp{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (2.44 GB cache), no flush"},
+            "seqs_per_s": nb / (step_ms * 1e-3),
+            "hbm_frac_of_measured_peak": value * 1e3 / peak,
+            "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
+                         "frac": achieved_gbs / peak, "traffic": traffic,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback 6650 GB/s",
+                         "kernel": "qmla_mla_decode call (plan + persistent decode + split merge), rank 0"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+            "gpu_launches": launches_per_step * args.steps + (1 if world > 1 else 0) * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=B,
+                    help="first N sequences of config1 (smaller cases for ncu captures; default: all 64)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

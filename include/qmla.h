@@ -3,9 +3,11 @@
  *
  * C ABI of libqmla.so.  Plain pointers and sizes only; every device pointer is
  * a CUDA device address, `stream` is a cudaStream_t passed as void*.  No entry
- * point allocates device memory, synchronises the device, or touches host
- * memory other than the parameter structs, so each one may be recorded into a
- * CUDA graph.  Entry points return 0 on success or a negative QMLA_E_* code.
+ * point allocates device memory or synchronises the device (qmla_read_status
+ * excepted), so the launching entry points may be recorded into a CUDA graph.
+ * Host-side the library keeps only per-device attributes and a small cache of
+ * TMA descriptors.  Entry points return 0 on success or a negative QMLA_E_*
+ * code.
  *
  * Reference interfaces replaced (paths inside sootaugur/qwen-mla-vllm):
  *   qmla_mla_decode   <- qwen_mla/ops/mla_decode_attention.py:1264-1359
@@ -39,7 +41,7 @@ extern "C" {
 #define QMLA_OK 0
 #define QMLA_E_INVALID (-1)        /* bad argument (null pointer, negative size, ...) */
 #define QMLA_E_UNSUPPORTED (-2)    /* shape / dtype combination this build has no kernel for */
-#define QMLA_E_ALIGNMENT (-3)      /* a pointer or stride breaks the 16-byte TMA rule */
+#define QMLA_E_ALIGNMENT (-3)      /* a cache pointer or stride is not 16-byte aligned */
 #define QMLA_E_WORKSPACE (-4)      /* workspace smaller than qmla_decode_workspace_bytes() */
 #define QMLA_E_CUDA (-5)           /* a CUDA runtime / driver call failed */
 #define QMLA_E_DEVICE_TIMEOUT (-6) /* a kernel gave up waiting (see qmla_read_status) */
@@ -74,9 +76,9 @@ typedef struct qmla_decode_params {
   const void* kv_cache;
   int64_t kv_stride_page, kv_stride_token;
   int64_t kv_num_pages;
-  int32_t kv_row_width; /* elements per row that may be read */
-  int32_t kv_dtype;     /* QMLA_DT_BF16, QMLA_DT_F16 or QMLA_DT_FP8E4M3 */
-  int32_t page_size;    /* tokens per page, a multiple of 16 */
+  int32_t kv_row_width; /* elements per row that may be read (>= qk_dim and rms tail) */
+  int32_t kv_dtype;     /* QMLA_DT_BF16 or QMLA_DT_FP8E4M3 (f16 caches: unsupported) */
+  int32_t page_size;    /* tokens per page (> 0); multiples of 16 use TMA boxes */
 
   /* block_table[row*block_table_stride + i] is the i-th page of a row;
    * seq_lens[row] its length in tokens (values < 0 are treated as 0). */

@@ -21,7 +21,7 @@ OK = 0
 ERRORS = {
     -1: "invalid argument",
     -2: "unsupported shape or dtype",
-    -3: "pointer or stride not 16-byte aligned for TMA",
+    -3: "pointer or stride not 16-byte aligned",
     -4: "workspace too small",
     -5: "CUDA call failed",
     -6: "device wait timed out",

@@ -4,7 +4,8 @@
 
 The library is a plain shared object (static CUDA runtime, no libcuda link:
 the TMA descriptor encoder is fetched at run time through the runtime's
-driver entry-point query), so it loads on machines without a GPU driver.
+driver entry-point query), so it loads on machines without a GPU driver and
+its host-only entry points (qmla_plan, ...) work there.
 """
 from __future__ import annotations
 

@@ -173,7 +173,10 @@ __global__ void dcp_merge_kernel(const uint8_t* parts, int parts_dt, const float
     float acc = 0.f;
     for (int n = 0; n < N; ++n) acc += expf(w_s[n] - m0);
     float g = logf(acc) + m0;
-    for (int n = 0; n < N; ++n) w_s[n] = expf(w_s[n] - g);
+    for (int n = 0; n < N; ++n) {
+      const float e = w_s[n] - g;  // NaN when every partial is empty: weight 0, as dcp_fix does
+      w_s[n] = (e != e || e == INFINITY) ? 0.f : expf(e);
+    }
     if (lse) lse[(int64_t)b * H + h] = g;
   }
   __syncthreads();

@@ -1,0 +1,117 @@
+"""Properties of the oracle that need no reference fixture: number formats against torch's
+own conversions, MTP flattening, and DCP split-and-merge consistency."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+
+def test_bf16_round_matches_torch():
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.standard_normal(20000).astype(np.float32) * 10.0 ** rng.integers(-30, 30, 20000),
+                        np.array([0.0, -0.0, 1.0, 65504.0, 3.4e38, -3.4e38, 1e-40, 1.00390625, 1.01171875],
+                                 dtype=np.float32)]).astype(np.float32)
+    want = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(oracle.f32_to_bf16_bits(x), want)
+
+
+def test_e4m3_encode_matches_torch_all_ranges():
+    rng = np.random.default_rng(1)
+    x = np.concatenate([
+        rng.uniform(-460, 460, 50000), rng.standard_normal(50000) * 1e-2,
+        rng.standard_normal(20000) * 2.0 ** -8,
+        # every midpoint between neighbouring codes (ties go to the even code)
+        (oracle.e4m3_decode(np.arange(126)) + oracle.e4m3_decode(np.arange(1, 127))) / 2,
+        -(oracle.e4m3_decode(np.arange(126)) + oracle.e4m3_decode(np.arange(1, 127))) / 2,
+        [0.0, -0.0, 448.0, -448.0, 2.0 ** -10, 2.0 ** -9, 3 * 2.0 ** -10]]).astype(np.float32)
+    x = np.clip(x, -448, 448).astype(np.float32)
+    want = torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    got = oracle.e4m3_encode(x)
+    assert np.array_equal(got, want), f"{int((got != want).sum())} codes differ"
+
+
+def test_e4m3_decode_matches_torch():
+    b = np.arange(256, dtype=np.uint8)
+    want = torch.from_numpy(b).view(torch.float8_e4m3fn).float().numpy()
+    got = oracle.e4m3_decode(b)
+    nan = np.isnan(want)
+    assert np.array_equal(np.isnan(got), nan)
+    assert np.array_equal(got[~nan], want[~nan])
+
+
+def test_log8_round_trip_error_bound():
+    x = np.exp2(np.linspace(-3, 3, 10001)).astype(np.float32)
+    back = oracle.log8_decode(oracle.log8_encode(x))
+    # one code step is 6/255 in log2: half a step bounds the relative error by 2^(3/255) - 1
+    assert np.max(np.abs(back / x - 1)) <= 2 ** (3 / 255) - 1 + 1e-6
+    assert oracle.log8_encode(np.array([1e-9, 0.0, 100.0], np.float32)).tolist() == [0, 0, 255]
+
+
+def test_mtp_flatten_lengths():
+    bt = np.arange(12, dtype=np.int32).reshape(3, 4)
+    lens = np.array([10, 2, 0], np.int32)
+    fbt, fl = oracle.mtp_flatten(bt, lens, 4)
+    assert fl.tolist() == [7, 8, 9, 10, 0, 0, 1, 2, 0, 0, 0, 0]
+    assert np.array_equal(fbt[5], bt[1]) and fbt.shape == (12, 4)
+
+
+def _rand_case(rng, B, H, rank, rope, page, lens):
+    W = rank + rope + H
+    W += (-W) % 8
+    pps = max(1, (max(lens) + page - 1) // page)
+    P = B * pps + 2
+    cache = oracle.f32_to_bf16_bits(rng.standard_normal((P, page, W)).astype(np.float32))
+    cache[..., rank + rope:] = oracle.f32_to_bf16_bits(rng.uniform(0.5, 2.0, (P, page, W - rank - rope)).astype(np.float32))
+    bt = rng.permutation(B * pps).reshape(B, pps).astype(np.int32)
+    q = oracle.bf16_round((rng.standard_normal((B, H, rank + rope)) / 32).astype(np.float32))
+    return cache, bt, q
+
+
+@pytest.mark.parametrize("n_shards", [2, 3, 8])
+def test_dcp_split_merge_equals_full(n_shards):
+    """Decoding contiguous KV shards and merging with the dcp_fix math reproduces the full decode."""
+    rng = np.random.default_rng(n_shards)
+    B, H, rank, rope, page = 3, 8, 128, 64, 16
+    lens = [300, 17, 1]
+    cache, bt, q = _rand_case(rng, B, H, rank, rope, page, lens)
+    kw = dict(rank=rank, qk_dim=rank + rope, page_size=page, sm_scale=1 / 16, rms_offset=rank + rope)
+    full_o, full_lse = oracle.decode(q, cache, bt, np.array(lens), **kw)
+    parts, lses = [], []
+    for s in range(n_shards):
+        # shard s owns tokens [lo, hi) of each row; present them as rows of their own
+        o_s, l_s = np.zeros_like(full_o), np.full_like(full_lse, -np.inf)
+        for b, L in enumerate(lens):
+            lo, hi = L * s // n_shards, L * (s + 1) // n_shards
+            if hi <= lo:
+                continue
+            t = np.arange(lo, hi)
+            rows = cache[bt[b, t // page], t % page]
+            sub = rows.reshape(1, hi - lo, -1)
+            ob, lb = oracle.decode(q[b:b + 1], sub, np.array([[0]]), np.array([hi - lo]),
+                                   **{**kw, "page_size": hi - lo})
+            o_s[b], l_s[b] = ob[0], lb[0]
+        parts.append(o_s)
+        lses.append(l_s)
+    o, lse = oracle.dcp_merge(np.stack(parts), np.stack(lses))
+    assert np.abs(o - full_o).max() < 1e-12
+    assert np.abs(lse - full_lse).max() < 1e-12
+
+
+def test_dcp_correct_special_values():
+    out = np.ones((1, 2, 4))
+    lses = np.array([[[np.nan, -np.inf]], [[0.0, -np.inf]]])
+    res, g = oracle.dcp_correct(out, lses, 0)
+    assert np.all(res[0, 0] == 0.0) and np.all(res[0, 1] == 0.0)
+    assert g[0, 0] == 0.0 and g[0, 1] == -np.inf
+    res1, _ = oracle.dcp_correct(out, lses, 1)
+    assert np.allclose(res1[0, 0], 1.0)
+
+
+def test_plan_arrays_edge_cases():
+    tp, indptr, kv_len = oracle.plan_arrays(np.array([0, -5, 1, 64, 65, 128]), 16)
+    assert tp.tolist() == [0, 0, 0, 1, 2, 4, 6]
+    assert indptr.tolist() == [0, 0, 0, 1, 5, 10, 18]
+    assert kv_len.tolist() == [0, 0, 1, 64, 65, 128]
