@@ -106,6 +106,10 @@ def load(path: os.PathLike | str | None = None) -> ctypes.CDLL:
     global _lib
     if _lib is not None and path is None:
         return _lib
+    if path is None and os.environ.get("QMLA_LIB_PATH"):
+        path = os.environ["QMLA_LIB_PATH"]  # an alternate build of the same ABI
+        if _lib is not None:
+            return _lib
     p = pathlib.Path(path) if path is not None else LIB_PATH
     if not p.exists():
         raise ImportError(f"libqmla.so not found at {p}: build it with "
@@ -116,7 +120,7 @@ def load(path: os.PathLike | str | None = None) -> ctypes.CDLL:
         fn = getattr(lib, name)
         fn.restype = res
         fn.argtypes = args
-    if path is None:
+    if path is None or os.environ.get("QMLA_LIB_PATH") == str(path):
         _lib = lib
     return lib
 

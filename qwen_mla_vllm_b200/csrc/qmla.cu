@@ -205,7 +205,7 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   const uint32_t q_bytes = pl->q_chunk * pl->n_sub_qk;
   pl->p_bytes = (uint32_t)(pl->npv * 128);
   const uint32_t misc_bytes = 4096;
-  const uint32_t rms_smem = pl->rms_units ? 2 * kTile * kRmsStride : 0;
+  const uint32_t rms_smem = (uint32_t)(2 * kTile * 16 * pl->rms_units);  // two staging buffers
   const uint32_t fixed = q_bytes + 2 * pl->p_bytes + misc_bytes + rms_smem + 1024 /*align slack*/;
   const int budget = std::min(di.max_smem, kMaxDynSmem) - (int)fixed;
   const int ns = budget / (int)slot_bytes;
@@ -448,7 +448,7 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
   if (cudaGetLastError() != cudaSuccess) return QMLA_E_CUDA;
   rc = launch_decode(p->kv_dtype == QMLA_DT_FP8E4M3, pl.nb, pl.nqk, tmap, a, pl.smem_total, st);
   if (rc != QMLA_OK) return rc;
-  split_merge_kernel<<<p->num_rows, 256, 0, st>>>(a);
+  split_merge_kernel<<<dim3(p->num_rows, p->num_heads), 128, 0, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
 }
 

@@ -60,63 +60,55 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
 
 // Merge of the per-CTA partial segments of rows that crossed a CTA boundary
 // (the reference's stage 2, mla_decode_attention.py:1064-1137, over the
-// decode kernel's partition).  One block per row.  Rows of length 0 get o = 0
-// and lse = -inf.
-__global__ void __launch_bounds__(256) split_merge_kernel(const DecodeArgs a) {
-  const int row = blockIdx.x;
+// decode kernel's partition).  One block per (row, head); rows inside one CTA
+// range are final already.  Rows of length 0 get o = 0 and lse = -inf.
+__global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
+  const int row = blockIdx.x, h = blockIdx.y;
   const int plo = __ldg(a.tile_prefix + row), phi = __ldg(a.tile_prefix + row + 1);
   const int total = __ldg(a.tile_prefix + a.num_rows);
   const int H = a.H, D = a.rank;
   const int osz = dt_size(a.o_dtype);
+  uint8_t* orow = a.o + ((int64_t)row * a.o_sr + (int64_t)h * a.o_sh) * osz;
   if (phi == plo) {
-    for (int i = threadIdx.x; i < H * D; i += blockDim.x) {
-      int h = i / D, d = i - h * D;
-      store_from_float(a.o + ((int64_t)row * a.o_sr + (int64_t)h * a.o_sh + d) * osz, a.o_dtype,
-                       0.f);
-    }
-    if (a.lse && threadIdx.x < H)
-      store_from_float(a.lse + ((int64_t)row * a.lse_sr + threadIdx.x) * dt_size(a.lse_dtype),
-                       a.lse_dtype, -INFINITY);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) store_from_float(orow + d * osz, a.o_dtype, 0.f);
+    if (a.lse && threadIdx.x == 0)
+      store_from_float(a.lse + ((int64_t)row * a.lse_sr + h) * dt_size(a.lse_dtype), a.lse_dtype,
+                       -INFINITY);
     return;
   }
   const int tpc = (total + a.G - 1) / a.G;
   const int c0 = plo / tpc, c1 = (phi - 1) / tpc;
   if (c0 == c1) return;  // the row lies inside one CTA range: already final
-  __shared__ float wts[32][kMaxCtas];
-  __shared__ float lse_g[32];
+  __shared__ float wts[kMaxCtas];
+  __shared__ int slots[kMaxCtas];
+  __shared__ float lse_g;
   const int np = c1 - c0 + 1;  // <= G <= kMaxCtas
-  // weights per (head, partial)
-  for (int h = threadIdx.x; h < H; h += blockDim.x) {
-    float m = -INFINITY;
-    for (int c = c0; c <= c1; ++c) {
-      int slot = (plo <= c * tpc) ? 2 * c : 2 * c + 1;
-      m = fmaxf(m, a.part_lse[(int64_t)slot * H + h]);
-    }
-    float s = 0.f;
-    for (int c = c0; c <= c1; ++c) {
-      int slot = (plo <= c * tpc) ? 2 * c : 2 * c + 1;
-      float w = (m == -INFINITY) ? 0.f : exp2f(a.part_lse[(int64_t)slot * H + h] - m);
-      wts[h][c - c0] = w;
-      s += w;
-    }
-    float inv = s > 0.f ? 1.f / s : 0.f;
-    for (int i = 0; i < np; ++i) wts[h][i] *= inv;
-    lse_g[h] = (m + log2f(s)) * kLn2;
+  for (int i = threadIdx.x; i < np; i += blockDim.x) {
+    const int c = c0 + i;
+    slots[i] = (plo <= c * tpc) ? 2 * c : 2 * c + 1;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < H * D; i += blockDim.x) {
-    int h = i / D, d = i - h * D;
-    float acc = 0.f;
-    for (int c = c0; c <= c1; ++c) {
-      int slot = (plo <= c * tpc) ? 2 * c : 2 * c + 1;
-      acc += wts[h][c - c0] * a.part_o[((int64_t)slot * H + h) * D + d];
+  if (threadIdx.x == 0) {
+    float m = -INFINITY;
+    for (int i = 0; i < np; ++i) m = fmaxf(m, a.part_lse[(int64_t)slots[i] * H + h]);
+    float sum = 0.f;
+    for (int i = 0; i < np; ++i) {
+      const float w = (m == -INFINITY) ? 0.f : exp2f(a.part_lse[(int64_t)slots[i] * H + h] - m);
+      wts[i] = w;
+      sum += w;
     }
-    store_from_float(a.o + ((int64_t)row * a.o_sr + (int64_t)h * a.o_sh + d) * osz, a.o_dtype,
-                     acc);
+    const float inv = sum > 0.f ? 1.f / sum : 0.f;
+    for (int i = 0; i < np; ++i) wts[i] *= inv;
+    lse_g = (m + log2f(sum)) * kLn2;
   }
-  if (a.lse && threadIdx.x < H)
-    store_from_float(a.lse + ((int64_t)row * a.lse_sr + threadIdx.x) * dt_size(a.lse_dtype),
-                     a.lse_dtype, lse_g[threadIdx.x]);
+  __syncthreads();
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+    for (int i = 0; i < np; ++i) acc += wts[i] * a.part_o[((int64_t)slots[i] * H + h) * D + d];
+    store_from_float(orow + d * osz, a.o_dtype, acc);
+  }
+  if (a.lse && threadIdx.x == 0)
+    store_from_float(a.lse + ((int64_t)row * a.lse_sr + h) * dt_size(a.lse_dtype), a.lse_dtype, lse_g);
 }
 
 // DCP output correction for one rank (qwen_mla/dcp_fix.py:31-98): grid (B, H).

@@ -45,18 +45,21 @@ constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
 constexpr int kWarpK = 8, kNumKWarps = 3, kWarpV = 11, kWarpQK = 12, kWarpPV = 14;
 constexpr int kNumWarps = 16, kNumThreads = kNumWarps * 32;
 constexpr int kKThreads = kNumKWarps * 32;
-constexpr int kRmsStride = 80;     // staging bytes per token: <= 64 rms bytes + 16-byte alignment
-constexpr int kRmsMaxUnits = kRmsStride / 16;
+constexpr int kRmsMaxUnits = 5;    // staged 16-byte units per token: <= 64 rms bytes + alignment
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P may reach 2^8 before O is rescaled
 constexpr int kBarSoftmax = 1;             // named barrier id of the softmax warps
 constexpr int kBarK = 2;                   // named barrier id of the K-load warps
 constexpr int kKdoneDepth = 8;             // QK-done signals in flight (V loads trail QK)
+// Tiles of a row bulk-prefetched into L2 ahead of the K loads (TMA mode).  Off: the
+// prefetches share the bulk-copy engine with the K boxes and evicted the latent lines
+// that the V loads re-read (DRAM bytes per launch rose from 1.07x to 1.47x of the
+// algorithmic bytes on config 1 and throughput fell 8%).
 #ifndef QMLA_PREFETCH_TILES
-#define QMLA_PREFETCH_TILES 2
+#define QMLA_PREFETCH_TILES 0
 #endif
-constexpr int kPrefetchTiles = QMLA_PREFETCH_TILES;  // tiles of a row prefetched into L2 ahead
+constexpr int kPrefetchTiles = QMLA_PREFETCH_TILES;
 
 struct DecodeArgs {
   // query
@@ -81,7 +84,7 @@ struct DecodeArgs {
   int n_qk_slots;   // 128-dim slots loaded per tile
   int n_sub_qk;     // 128-byte-wide MMA sub-chunks of the QK width
   int rms_base_b;   // 16-byte-aligned first byte of the rms tail in a row
-  int rms_units;    // 16-byte units staged per token (0: no rms)
+  int rms_units;    // 16-byte units staged per token (0: no rms); staging stride = 16 * rms_units
   int rms_skip;     // first rms byte within the staged units
   int pf_bytes;     // bytes of a cache row prefetched into L2 (QK columns + rms tail)
   float sm_scale;
@@ -308,7 +311,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       mbar_init(bar(b_kempty + i), KP);
     }
     for (uint32_t i = 0; i < nv; ++i) {
-      mbar_init(bar(b_vfull + i), 32);
+      mbar_init(bar(b_vfull + i), a.use_tma ? 64 : 32);  // V-load threads
       mbar_init(bar(b_vempty + i), 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -316,7 +319,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       mbar_init(bar(b_sempty + i), kSoftmaxWarps);
       mbar_init(bar(b_pfull + i), kSoftmaxWarps);
       mbar_init(bar(b_odone + i), 2);
-      mbar_init(bar(b_rfull + i), a.use_tma ? kKThreads - 32 : kKThreads);
+      mbar_init(bar(b_rfull + i), a.use_tma ? 32 : kKThreads);
       mbar_init(bar(b_rempty + i), kSoftmaxWarps);
     }
     for (int i = 0; i < kKdoneDepth; ++i) mbar_init(bar(b_kdone + i), KP);
@@ -341,7 +344,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t vring = sbase + a.off_vring;
   const uint32_t qbuf = sbase + a.off_q;
   const uint32_t pbuf = sbase + a.off_p;
-  const uint32_t rmsbuf = sbase + a.off_rms;  // [2][64 tokens][kRmsStride]
+  const uint32_t rmsbuf = sbase + a.off_rms;  // [2][64 tokens][rstride]
+  const int rstride = 16 * a.rms_units;       // rms staging bytes per token
   int* status = a.status;
 
   if (a.use_tma && warp == kWarpK) {
@@ -364,15 +368,18 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       int L = __ldg(a.seq_lens + row);
       L = L < 0 ? 0 : L;
       const int32_t* bt = a.block_table + (int64_t)row * a.bt_stride;
+      // page of token run `lane` of a tile (-1: past the row end, loads zeros)
+      auto run_page = [&](int k) -> int {
+        const int tok = k * kTile + lane * run;
+        return (lane < nrun && tok < L) ? __ldg(bt + tok / a.page_size) : -1;
+      };
+      int pg = run_page(k0);
       for (int k = k0; k < k1 && ok; ++k, ++jt) {
-        int pg = -1;  // page of token run `lane`; runs past the row end load zeros
-        if (lane < nrun) {
-          const int tok = k * kTile + lane * run;
-          if (tok < L) pg = __ldg(bt + tok / a.page_size);
-        }
         const int mypg = __shfl_sync(0xffffffffu, pg, bg);
         const int y = (k * kTile + bg * run) % a.page_size;
+        int pg_next = -1;  // the next tile's page ids load while this tile's slots issue
         for (int s = 0; s < a.n_qk_slots && ok; ++s) {
+          if (s == 0 && k + 1 < k1) pg_next = run_page(k + 1);
           if (lane == 0) {
             ok = mbar_wait(bar(b_kempty + r.idx), r.ph ^ 1, abort_flag, status);
             if (ok) mbar_expect_tx(bar(b_kfull + r.idx), (uint32_t)kSlotBytes);
@@ -390,6 +397,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           if (lane == 0) QMLA_TRS(1, s);
           r.next(nk);
         }
+        pg = pg_next;
       }
     }
     // After an abort: wait (bounded) for the boxes already issued, so no copy still
@@ -401,9 +409,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
     }
     __syncwarp();
-  } else if (a.use_tma && warp > kWarpK && warp < kWarpK + kNumKWarps) {
+  } else if (a.use_tma && warp == kWarpK + 1) {
     // ====================================================== rms tail + L2 prefetch (TMA mode)
-    const int pt = threadIdx.x - (kWarpK + 1) * 32;  // 0..63: one token of the tile each
+    // One warp; lane handles tokens `lane` and `lane + 32` of each tile.
     const uint64_t pol_lat = policy_evict_normal();
     const uint64_t pol_rope = policy_evict_first();
     SegCursor cur{row0, range_lo, range_hi};
@@ -414,35 +422,42 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       int L = __ldg(a.seq_lens + row);
       L = L < 0 ? 0 : L;
       const int32_t* bt = a.block_table + (int64_t)row * a.bt_stride;
-      for (int kp = k0; kp < min(k1, k0 + kPrefetchTiles); ++kp) {
-        const uint64_t pa = token_row_addr(a, bt, L, kp, pt);
-        if (pa) bulk_prefetch_l2(reinterpret_cast<const void*>(pa), a.pf_bytes, pol_lat);
+      for (int kp = k0; kp < min(k1, k0 + kPrefetchTiles); ++kp) {  // no-op unless enabled
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const uint64_t pa = token_row_addr(a, bt, L, kp, lane + 32 * h2);
+          if (pa) bulk_prefetch_l2(reinterpret_cast<const void*>(pa), a.pf_bytes, pol_lat);
+        }
       }
       for (int k = k0; k < k1 && ok; ++k, ++jt) {
-        if (k + kPrefetchTiles < k1) {
-          const uint64_t pa = token_row_addr(a, bt, L, k + kPrefetchTiles, pt);
-          if (pa) bulk_prefetch_l2(reinterpret_cast<const void*>(pa), a.pf_bytes, pol_lat);
+        if (kPrefetchTiles > 0 && k + kPrefetchTiles < k1) {
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const uint64_t pa = token_row_addr(a, bt, L, k + kPrefetchTiles, lane + 32 * h2);
+            if (pa) bulk_prefetch_l2(reinterpret_cast<const void*>(pa), a.pf_bytes, pol_lat);
+          }
         }
         if (a.rms_units > 0) {
           const uint32_t tb = jt & 1;
           if (jt >= 2) ok = mbar_wait(bar(b_rempty + tb), ((jt - 2) >> 1) & 1, abort_flag, status);
+          ok = __all_sync(0xffffffffu, ok);
           if (ok) {
-            const uint64_t src = token_row_addr(a, bt, L, k, pt);
-            for (int u = 0; u < a.rms_units; ++u) {
-              const int col = a.rms_base_b + 16 * u;
-              const int nbytes = src ? max(0, min(16, a.row_bytes - col)) : 0;
-              cp_async_16_hint(rmsbuf + tb * (kTile * kRmsStride) + pt * kRmsStride + 16 * u,
-                               nbytes ? reinterpret_cast<const void*>(src + col) : a.cache,
-                               (uint32_t)nbytes, pol_rope);
+            for (int h2 = 0; h2 < 2; ++h2) {
+              const int t = lane + 32 * h2;
+              const uint64_t src = token_row_addr(a, bt, L, k, t);
+              for (int u = 0; u < a.rms_units; ++u) {
+                const int col = a.rms_base_b + 16 * u;
+                const int nbytes = src ? max(0, min(16, a.row_bytes - col)) : 0;
+                cp_async_16_hint(rmsbuf + tb * (kTile * rstride) + t * rstride + 16 * u,
+                                 nbytes ? reinterpret_cast<const void*>(src + col) : a.cache,
+                                 (uint32_t)nbytes, pol_rope);
+              }
             }
             cp_async_mbar_arrive(bar(b_rfull + tb));
           }
         }
-        ok = !named_bar_or(kBarK, kKThreads - 32, !ok);
       }
     }
     if (!ok) asm volatile("cp.async.wait_all;" ::: "memory");
-  } else if (warp >= kWarpK && warp < kWarpK + kNumKWarps) {
+  } else if (!a.use_tma && warp >= kWarpK && warp < kWarpK + kNumKWarps) {
     // ====================================================== K loads by cp.async (+ rms tail)
     const int pt = threadIdx.x - kWarpK * 32;  // 0..95
     const uint64_t pol_lat = policy_evict_normal();  // latent columns: read again for PV
@@ -460,8 +475,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       L = L < 0 ? 0 : L;
       const int32_t* bt = a.block_table + (int64_t)row * a.bt_stride;
       uint64_t nptr = pt < 64 ? token_row_addr(a, bt, L, k0, pt) : 0ull;
-      // L2 prefetch runs kPrefetchTiles ahead of the loads, so the DRAM requests
-      // in flight are not bounded by the shared-memory ring
+      // optional L2 prefetch kPrefetchTiles ahead of the loads (off by default)
       if (pt < 64) {
         for (int kp = k0; kp < min(k1, k0 + kPrefetchTiles); ++kp) {
           const uint64_t pa = kp == k0 ? nptr : token_row_addr(a, bt, L, kp, pt);
@@ -472,7 +486,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const uint32_t tb = jt & 1;
         if (pt < 64) tokptr[tb * 64 + pt] = nptr;
         named_bar_sync(kBarK, kKThreads);
-        if (pt < 64 && k + kPrefetchTiles < k1) {
+        if (kPrefetchTiles > 0 && pt < 64 && k + kPrefetchTiles < k1) {
           const uint64_t pa = token_row_addr(a, bt, L, k + kPrefetchTiles, pt);
           if (pa) bulk_prefetch_l2(reinterpret_cast<const void*>(pa), a.pf_bytes, pol_lat);
         }
@@ -487,7 +501,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
               const uint64_t src = tp[t];
               const int col = a.rms_base_b + 16 * u;
               const int nbytes = src ? max(0, min(16, a.row_bytes - col)) : 0;
-              cp_async_16_hint(rmsbuf + tb * (kTile * kRmsStride) + t * kRmsStride + 16 * u,
+              cp_async_16_hint(rmsbuf + tb * (kTile * rstride) + t * rstride + 16 * u,
                                nbytes ? reinterpret_cast<const void*>(src + col) : a.cache,
                                (uint32_t)nbytes, pol_rope);
             }
@@ -525,9 +539,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
     }
     if (!ok) asm volatile("cp.async.wait_all;" ::: "memory");
-  } else if (warp == kWarpV) {
+  } else if (warp == kWarpV || (a.use_tma && warp == kWarpK + 2)) {
     // ====================================================== V loads by cp.async (from L2)
+    // One warp (cp.async mode) or two (TMA mode, where warp 10 is free): warp vw of nvw
+    // gathers tokens [vw * 64/nvw, (vw + 1) * 64/nvw) of each latent block.
     const uint64_t pol = policy_evict_first();
+    const int nvw = a.use_tma ? 2 : 1;
+    const int vw = warp == kWarpV ? nvw - 1 : 0;
+    const int tpw = kTile / nvw;  // tokens per V warp
+    constexpr int kTokStep = 32 / kUnitsPerRow;  // tokens per warp-wide copy step
     SegCursor cur{row0, range_lo, range_hi};
     int row, k0, k1, plo, phi;
     uint32_t jt = 0;
@@ -538,49 +558,37 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       L = L < 0 ? 0 : L;
       const int32_t* bt = a.block_table + (int64_t)row * a.bt_stride;
       for (int k = k0; k < k1 && ok; ++k, ++jt) {
-        const uint64_t p0 = token_row_addr(a, bt, L, k, lane);  // this lane's two tokens
-        const uint64_t p1 = token_row_addr(a, bt, L, k, lane + 32);
+        // this lane's tokens: vw*tpw + lane (and + 32 when one warp covers the tile)
+        const uint64_t p0 = token_row_addr(a, bt, L, k, vw * tpw + lane);
+        const uint64_t p1 = tpw > 32 ? token_row_addr(a, bt, L, k, vw * tpw + lane + 32) : 0ull;
         // the latent part is read again only after QK(jt) consumed it (it is in L2)
         ok = mbar_wait(bar(b_kdone + (jt % kKdoneDepth)), (jt / kKdoneDepth) & 1, abort_flag,
                        status);
         ok = __all_sync(0xffffffffu, ok);
-        if (lane == 0) QMLA_TR(6);
+        if (lane == 0 && vw == 0) QMLA_TR(6);
         for (int b = 0; b < NB && ok; ++b) {
           ok = mbar_wait(bar(b_vempty + r.idx), r.ph ^ 1, abort_flag, status);
           ok = __all_sync(0xffffffffu, ok);
           if (ok) {
             const uint32_t dst0 = vring + r.idx * kSlotBytes;
-            if constexpr (!FP8) {
-              // 64 tokens x 16 units: two tokens per warp step
-              const int u = lane & 15, sc = u >> 3, v = u & 7;
-              const int colb = (b * 128 + sc * 64 + v * 8) * 2;
+            const int u = lane % kUnitsPerRow, sc = u >> 3, v = u & 7;
+            const int colb = FP8 ? b * 128 + v * 16 : (b * 128 + sc * 64 + v * 8) * 2;
+            const int steps = tpw / kTokStep;
 #pragma unroll 8
-              for (int i = 0; i < 32; ++i) {
-                const int t = 2 * i + (lane >> 4);
-                const uint64_t src = __shfl_sync(0xffffffffu, i < 16 ? p0 : p1, t & 31);
-                cp_async_16_hint(dst0 + sc * 8192 + t * 128 + ((v ^ (t & 7)) << 4),
-                                 src ? reinterpret_cast<const void*>(src + colb) : a.cache,
-                                 src ? 16u : 0u, pol);
-              }
-            } else {
-              // 64 tokens x 8 units: four tokens per warp step
-              const int v = lane & 7;
-              const int colb = b * 128 + v * 16;
-#pragma unroll 8
-              for (int i = 0; i < 16; ++i) {
-                const int t = 4 * i + (lane >> 3);
-                const uint64_t src = __shfl_sync(0xffffffffu, i < 8 ? p0 : p1, t & 31);
-                cp_async_16_hint(dst0 + t * 128 + ((v ^ (t & 7)) << 4),
-                                 src ? reinterpret_cast<const void*>(src + colb) : a.cache,
-                                 src ? 16u : 0u, pol);
-              }
+            for (int i = 0; i < steps; ++i) {
+              const int tl = i * kTokStep + lane / kUnitsPerRow;  // token within this warp's part
+              const uint64_t src = __shfl_sync(0xffffffffu, i * kTokStep < 32 ? p0 : p1, tl & 31);
+              const int t = vw * tpw + tl;
+              cp_async_16_hint(dst0 + sc * 8192 + t * 128 + ((v ^ (t & 7)) << 4),
+                               src ? reinterpret_cast<const void*>(src + colb) : a.cache,
+                               src ? 16u : 0u, pol);
             }
             cp_async_mbar_arrive(bar(b_vfull + r.idx));
           }
-          if (lane == 0) QMLA_TRS(3, b);
+          if (lane == 0 && vw == 0) QMLA_TRS(3, b);
           r.next(nv);
         }
-        if (lane == 0) QMLA_TR(13);
+        if (lane == 0 && vw == 0) QMLA_TR(13);
       }
     }
     if (!ok) asm volatile("cp.async.wait_all;" ::: "memory");
@@ -882,7 +890,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           ok = mbar_wait(bar(b_rfull + pb), (jt >> 1) & 1, abort_flag, status);
           if (ok) {
             if (valid) {
-              const uint8_t* rp = rms_smem + pb * (kTile * kRmsStride) + tt * kRmsStride + a.rms_skip;
+              const uint8_t* rp = rms_smem + pb * (kTile * rstride) + tt * rstride + a.rms_skip;
 #pragma unroll
               for (int j = 0; j < NJ; ++j) {
                 if (head[j] < H) {

@@ -236,9 +236,14 @@ def test_errors_are_raised(cuda_device):
     o = torch.zeros(1, 24, 768, dtype=torch.bfloat16, device=cuda_device)
     p = build_params(q, cache, o, None, bt, sl, rank=768, qk_dim=1000, rms_offset=1000, rms_mode=1,
                      page_size=16, sm_scale=1 / 16)
-    with pytest.raises(_lib.QmlaError) as e:
+    with pytest.raises(ValueError, match="workspace"):
         run_params(p, cuda_device, workspace=torch.empty(64, dtype=torch.uint8, device=cuda_device))
-    assert e.value.code in (-4, -3)
+    # the C entry point itself rejects a short workspace
+    import ctypes
+    ws = torch.empty(256, dtype=torch.uint8, device=cuda_device)
+    p.workspace, p.workspace_bytes = ws.data_ptr(), 256
+    rc = _lib.load().qmla_mla_decode(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == -4
     # rank 1792 (NB = 14) has no kernel in this build
     big = torch.zeros(4, 16, 1, 2048, dtype=torch.bfloat16, device=cuda_device)
     q2 = torch.zeros(1, 24, 2048, dtype=torch.bfloat16, device=cuda_device)
