@@ -210,13 +210,15 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   const int budget = std::min(di.max_smem, kMaxDynSmem) - (int)fixed;
   const int ns = budget / (int)slot_bytes;
   if (ns < 2) return QMLA_E_UNSUPPORTED;
-  // K ring: the HBM stream (bandwidth x latency); V ring: L2 re-reads for PV
-  int nk = std::max(1, std::min((ns * 11 + 19) / 20, 3 * pl->n_qk_slots));
   // A PV issuer skips the other issuer's blocks of each tile, so it may wait on a
   // V slot up to max(NB0, NB - NB0) positions after the last one it saw filled;
   // one more slot than that keeps every parity wait within one phase.
   const int nb0 = (nb + 1) / 2;
   const int nv_min = std::max(nb0, nb - nb0) + 1;
+  if (ns < nv_min + 1) return QMLA_E_UNSUPPORTED;
+  // K ring: the HBM stream (bandwidth x latency); V ring: L2 re-reads for PV
+  int nk = std::min((ns * 11 + 19) / 20, 3 * pl->n_qk_slots);
+  nk = std::max(1, std::min(nk, ns - nv_min));
   int nv = std::max(nv_min, std::min(ns - nk, 2 * nb));
   // test hooks: QMLA_NK / QMLA_NV override the ring sizes (clamped to legal values)
   if (const char* e = getenv("QMLA_NK")) nk = std::max(1, std::min(atoi(e), ns - nv_min));

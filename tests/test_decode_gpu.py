@@ -108,7 +108,8 @@ def test_fp8_modes(cuda_device, mode, page):
     compare(o, lse, ref_o, ref_lse, tol=FP8_TOL, rel_tol=2e-2)
 
 
-@pytest.mark.parametrize("heads,rank,rope", [(12, 384, 116), (16, 512, 128), (32, 256, 232), (8, 768, 232)])
+@pytest.mark.parametrize("heads,rank,rope", [(12, 384, 116), (16, 512, 128), (32, 256, 232), (8, 768, 232),
+                                             (32, 768, 232)])
 def test_head_and_rank_shapes(cuda_device, heads, rank, rope):
     """GLA-g2 groups (12 heads, 384 | 116) and the other head counts / ranks the kernel is built for."""
     lens = [300, 4097, 5]
