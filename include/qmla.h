@@ -128,6 +128,14 @@ int qmla_decode_workspace_bytes(const qmla_decode_params* p, int64_t* bytes);
  * kernel on `stream`. */
 int qmla_mla_decode(const qmla_decode_params* p, void* stream);
 
+/* qmla_mla_decode without a caller workspace (no reference counterpart: the reference's
+ * decode always receives vLLM-owned scratch).  Uses a 32 MiB device array inside the library
+ * (one per device, its address looked up once); shapes whose workspace would exceed it return
+ * QMLA_E_WORKSPACE.  No device memory is allocated.  Calls on one device share that array:
+ * two calls whose executions overlap (different streams, or graphs replayed concurrently)
+ * race on it, so callers must order them (one stream, or events). */
+int qmla_mla_decode_static(const qmla_decode_params* p, void* stream);
+
 /* Device status word of the last call that used `workspace`: 0, or bit 0 set
  * when a kernel wait timed out.  Copies 4 bytes device->host on `stream` and
  * synchronises that stream (host-side diagnostic, not for graph capture). */

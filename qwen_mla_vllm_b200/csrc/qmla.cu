@@ -312,6 +312,23 @@ int launch_decode(bool fp8, int nb, int nqk, const CUtensorMap& tmap, const Deco
 unsigned long long* g_trace = nullptr;
 #endif
 
+// Scratch for qmla_mla_decode_static: a fixed device array instead of a caller workspace.
+// 32 MiB covers the decode workspace up to 160 CTAs x 32 heads x rank 768 (31.5 MB of fp32
+// partials) with up to 16383 rows.  One array per device, shared by every call on it.
+constexpr int64_t kStaticScratchBytes = int64_t(32) << 20;
+__device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+std::map<int, void*> g_static_addr;  // device -> address of g_static_scratch (looked up once)
+
+void* static_scratch(int dev) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_static_addr.find(dev);
+  if (it != g_static_addr.end()) return it->second;
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess) return nullptr;
+  g_static_addr[dev] = p;
+  return p;
+}
+
 }  // namespace
 
 extern "C" {
@@ -452,6 +469,25 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
   if (rc != QMLA_OK) return rc;
   split_merge_kernel<<<dim3(p->num_rows, p->num_heads), 128, 0, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
+}
+
+int qmla_mla_decode_static(const qmla_decode_params* p, void* stream) {
+  if (!p) return QMLA_E_INVALID;
+  int64_t need = 0;
+  int rc = qmla_decode_workspace_bytes(p, &need);
+  if (rc != QMLA_OK) return rc;
+  if (need > kStaticScratchBytes) return QMLA_E_WORKSPACE;
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess) return QMLA_E_CUDA;
+  if (cur != p->device && cudaSetDevice(p->device) != cudaSuccess) return QMLA_E_CUDA;
+  void* scratch = static_scratch(p->device);
+  if (!scratch) return QMLA_E_CUDA;
+  // Same launch sequence as qmla_mla_decode; its plan kernel (or the memset taken with a
+  // precomputed plan) clears the status word, the only scratch that must start at zero.
+  qmla_decode_params q = *p;
+  q.workspace = scratch;
+  q.workspace_bytes = kStaticScratchBytes;
+  return qmla_mla_decode(&q, stream);
 }
 
 int qmla_read_status(const void* workspace, void* stream, int32_t* status) {
