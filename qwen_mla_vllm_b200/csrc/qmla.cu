@@ -177,11 +177,10 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
     end = std::min<int64_t>(align_up(end, 16), p->kv_stride_token * es);
     pl->pf_bytes = (int)end;
   }
-  // slots are 128 dims (elements of a bf16 row, bytes of an FP8 row)
-  pl->n_qk_slots = (p->qk_dim + 127) / 128;
-  pl->n_sub_qk = fp8 ? pl->n_qk_slots : (p->qk_dim + 63) / 64;
+  // K slots hold 256 bytes of each token's row (two 128-byte MMA sub-chunks)
+  pl->n_qk_slots = (pl->qk_bytes + 255) / 256;
+  pl->n_sub_qk = (pl->qk_bytes + 127) / 128;
   if (pl->n_sub_qk > kMaxQkChunks) return QMLA_E_UNSUPPORTED;
-  if (pl->n_qk_slots < nb) return QMLA_E_INVALID;
   // 16-byte vector loads of q rows (bf16 only; element strides in 2-byte units)
   auto vec_ok = [](const void* ptr, int64_t sr, int64_t sh) {
     return reinterpret_cast<uintptr_t>(ptr) % 16 == 0 && (sr * 2) % 16 == 0 && (sh * 2) % 16 == 0;
@@ -199,7 +198,8 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   pl->G = G;
 
   // shared memory map: K ring, V ring, Q, 2 P buffers, 2 rms staging buffers, misc
-  const uint32_t slot_bytes = fp8 ? 8192u : 16384u;
+  const uint32_t kslot = 16384u;              // 64 tokens x 256 bytes
+  const uint32_t vslot = fp8 ? 8192u : 16384u;  // 64 tokens x 128 dims
   const int q_rows = fp8 ? 2 * pl->nqk : pl->nqk;
   pl->q_chunk = (uint32_t)((q_rows + 7) / 8 * 1024);
   const uint32_t q_bytes = pl->q_chunk * pl->n_sub_qk;
@@ -208,32 +208,31 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   const uint32_t rms_smem = (uint32_t)(2 * kTile * 16 * pl->rms_units);  // two staging buffers
   const uint32_t fixed = q_bytes + 2 * pl->p_bytes + misc_bytes + rms_smem + 1024 /*align slack*/;
   const int budget = std::min(di.max_smem, kMaxDynSmem) - (int)fixed;
-  const int ns = budget / (int)slot_bytes;
-  if (ns < 2) return QMLA_E_UNSUPPORTED;
   // A PV issuer skips the other issuer's blocks of each tile, so it may wait on a
   // V slot up to max(NB0, NB - NB0) positions after the last one it saw filled;
   // one more slot than that keeps every parity wait within one phase.
   const int nb0 = (nb + 1) / 2;
   const int nv_min = std::max(nb0, nb - nb0) + 1;
-  if (ns < nv_min + 1) return QMLA_E_UNSUPPORTED;
-  // K ring: the HBM stream (bandwidth x latency); V ring: L2 re-reads for PV
-  int nk = std::min((ns * 11 + 19) / 20, 3 * pl->n_qk_slots);
-  nk = std::max(1, std::min(nk, ns - nv_min));
-  int nv = std::max(nv_min, std::min(ns - nk, 2 * nb));
+  if (budget < (int)(kslot + nv_min * vslot)) return QMLA_E_UNSUPPORTED;
+  // K ring: the HBM stream (bandwidth x latency), ~55% of the rings; V ring: L2 re-reads for PV
+  const int nk_max = (budget - nv_min * (int)vslot) / (int)kslot;
+  int nk = std::min(((budget * 11 / 20) + (int)kslot - 1) / (int)kslot, 3 * pl->n_qk_slots);
+  nk = std::max(1, std::min(nk, nk_max));
   // test hooks: QMLA_NK / QMLA_NV override the ring sizes (clamped to legal values)
-  if (const char* e = getenv("QMLA_NK")) nk = std::max(1, std::min(atoi(e), ns - nv_min));
-  nv = std::max(nv_min, std::min(nv, ns - nk));
-  if (const char* e = getenv("QMLA_NV")) nv = std::max(nv_min, std::min(atoi(e), ns - nk));
-  if (nk + nv > ns) return QMLA_E_UNSUPPORTED;
+  if (const char* e = getenv("QMLA_NK")) nk = std::max(1, std::min(atoi(e), nk_max));
+  int nv = std::min((budget - nk * (int)kslot) / (int)vslot, 2 * nb);
+  if (const char* e = getenv("QMLA_NV")) nv = std::min(atoi(e), nv);
+  nv = std::max(nv, nv_min);
+  if (nk * (int)kslot + nv * (int)vslot > budget) return QMLA_E_UNSUPPORTED;
   pl->nk = (uint32_t)nk;
   pl->nv = (uint32_t)nv;
   const uint32_t n_bars = 2 * (pl->nk + pl->nv) + 14 + kKdoneDepth + 4;
   if ((n_bars * 8 + 15) / 16 * 16 + 16 + 1024 + 512 + 1024 > misc_bytes) return QMLA_E_UNSUPPORTED;
   uint32_t off = 0;
   pl->off_kring = off;
-  off += pl->nk * slot_bytes;
+  off += pl->nk * kslot;
   pl->off_vring = off;
-  off += pl->nv * slot_bytes;
+  off += pl->nv * vslot;
   pl->off_q = off;
   off += q_bytes;
   pl->off_p = off;
@@ -447,6 +446,7 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
   a.off_misc = pl.off_misc;
 #ifdef QMLA_TRACE
   a.trace = g_trace;
+  a.trace_cta = getenv("QMLA_TRACE_CTA") ? (unsigned)atoi(getenv("QMLA_TRACE_CTA")) : 0u;
 #else
   a.trace = nullptr;
 #endif

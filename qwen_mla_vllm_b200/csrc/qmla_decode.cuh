@@ -81,7 +81,7 @@ struct DecodeArgs {
   int num_rows, H, rank, qk_dim, rms_mode;
   int qk_bytes;     // bytes of a cache row the QK contraction reads
   int row_bytes;    // bytes of a cache row (kv_row_width * element size)
-  int n_qk_slots;   // 128-dim slots loaded per tile
+  int n_qk_slots;   // K-ring slots loaded per tile (256 bytes of each token's row per slot)
   int n_sub_qk;     // 128-byte-wide MMA sub-chunks of the QK width
   int rms_base_b;   // 16-byte-aligned first byte of the rms tail in a row
   int rms_units;    // 16-byte units staged per token (0: no rms); staging stride = 16 * rms_units
@@ -108,16 +108,17 @@ struct DecodeArgs {
   // Optional stage timestamps of CTA 0 (builds with -DQMLA_TRACE only):
   // trace[tile * 16 + event] = %globaltimer in ns.
   unsigned long long* trace;
+  unsigned trace_cta;  // the CTA whose stages are traced
 };
 
 #ifdef QMLA_TRACE
 #define QMLA_TR(ev)                                                                            \
   do {                                                                                         \
-    if (a.trace && blockIdx.x == 0 && jt < 256) a.trace[jt * 16 + (ev)] = globaltimer_ns(); \
+    if (a.trace && blockIdx.x == a.trace_cta && jt < 256) a.trace[jt * 16 + (ev)] = globaltimer_ns(); \
   } while (0)
 #define QMLA_TRS(plane, idx)                                                     \
   do {                                                                           \
-    if (a.trace && blockIdx.x == 0 && jt < 256)                                  \
+    if (a.trace && blockIdx.x == a.trace_cta && jt < 256)                        \
       a.trace[(plane) * 4096 + jt * 16 + (idx)] = globaltimer_ns();              \
   } while (0)
 #else
@@ -243,9 +244,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     mla_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
   static_assert(NQK % 8 == 0 && NQK >= 8 && NQK <= 32, "heads rounded to 8..32");
   constexpr int NPV = NQK <= 16 ? 16 : 32;        // PV MMA N (multiple of 16)
-  constexpr int kSlotBytes = FP8 ? 8192 : 16384;  // 64 tokens x 128 dims
-  constexpr int kSubs = FP8 ? 1 : 2;              // 128-byte-wide sub-chunks per slot
-  constexpr int kUnitsPerRow = kSubs * 8;         // 16-byte units per token per slot
+  // K ring slot: 64 tokens x 256 bytes of the row (128 bf16 / 256 e4m3 dims), two 128-byte
+  // swizzled sub-chunks.  V ring slot: 64 tokens x one 128-dim output block.
+  constexpr int kKSlotBytes = 16384;
+  constexpr int kKSubs = 2;
+  constexpr int kKUnits = kKSubs * 8;             // 16-byte units per token per K slot
+  constexpr int kVSlotBytes = FP8 ? 8192 : 16384;
+  constexpr int kVUnits = (FP8 ? 1 : 2) * 8;      // 16-byte units per token per V slot
   constexpr int OW = NPV;                         // TMEM columns per O block
   constexpr int SWP = FP8 ? 2 * NPV : NPV;        // TMEM columns per S partial (hi|lo for FP8)
   constexpr int KP = 2;                           // S partials (one per QK issuer)
@@ -260,7 +265,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   constexpr int kPvSteps = FP8 ? 2 : 4;  // K = 32 (e4m3) or 16 (bf16) tokens per PV MMA
   constexpr int kPvAStep = FP8 ? 4096 : 2048;
   constexpr int kPvBStep = (FP8 ? 4 : 2) * 16 * NPV;
-  constexpr int kKTokStep = kKThreads / kUnitsPerRow;  // tokens between a K thread's copies
+  constexpr int kKTokStep = kKThreads / kKUnits;  // tokens between a K thread's copies
   constexpr int kKIters = (kTile + kKTokStep - 1) / kKTokStep;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -277,6 +282,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const int range_hi = min(total, range_lo + tpc);
   if (range_lo >= range_hi) return;  // uniform for the whole CTA
   const int row0 = first_row_at(a.tile_prefix, a.num_rows, range_lo);
+#ifdef QMLA_TRACE
+  if (a.trace && threadIdx.x == 0) {
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    a.trace[6 * 4096 + blockIdx.x * 2] = globaltimer_ns();
+    a.trace[6 * 4096 + 2048 + blockIdx.x] = smid;
+  }
+#endif
 
   // ------------------------------------------------ barriers and scratch
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + a.off_misc);
@@ -355,7 +368,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // and pages outside the cache are zero-filled by the tensor map bounds.
     const uint64_t pol_lat = policy_evict_normal();
     const uint64_t pol_rope = policy_evict_first();
-    const int run = a.run_rows, nrun = kTile / run, nbox = kSubs * nrun;
+    const int run = a.run_rows, nrun = kTile / run, nbox = kKSubs * nrun;
     const int xstep = FP8 ? 128 : 64;  // box width in elements
     const int bsc = lane / nrun, bg = lane % nrun;  // this lane's box: sub-chunk, token run
     if (lane == 0) prefetch_tmap(&tmap);
@@ -382,15 +395,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           if (s == 0 && k + 1 < k1) pg_next = run_page(k + 1);
           if (lane == 0) {
             ok = mbar_wait(bar(b_kempty + r.idx), r.ph ^ 1, abort_flag, status);
-            if (ok) mbar_expect_tx(bar(b_kfull + r.idx), (uint32_t)kSlotBytes);
+            if (ok) mbar_expect_tx(bar(b_kfull + r.idx), (uint32_t)kKSlotBytes);
             QMLA_TRS(4, s);
             if (s == 0) QMLA_TR(0);
           }
           ok = __shfl_sync(0xffffffffu, ok, 0);
           if (ok) {
             if (lane < nbox)
-              tma_load_3d(kring + r.idx * kSlotBytes + bsc * 8192 + bg * run * 128, &tmap,
-                          (kSubs * s + bsc) * xstep, y, mypg, bar(b_kfull + r.idx),
+              tma_load_3d(kring + r.idx * kKSlotBytes + bsc * 8192 + bg * run * 128, &tmap,
+                          (kKSubs * s + bsc) * xstep, y, mypg, bar(b_kfull + r.idx),
                           s < NB ? pol_lat : pol_rope);
             ++armed;
           }
@@ -462,8 +475,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const int pt = threadIdx.x - kWarpK * 32;  // 0..95
     const uint64_t pol_lat = policy_evict_normal();  // latent columns: read again for PV
     const uint64_t pol_rope = policy_evict_first();  // rope columns: read once
-    const int ku = pt % kUnitsPerRow;                // this thread's 16-byte column unit
-    const int kt0 = pt / kUnitsPerRow;               // and first token
+    const int ku = pt % kKUnits;                     // this thread's 16-byte column unit
+    const int kt0 = pt / kKUnits;                    // and first token
     const int ksc = ku >> 3, kv = ku & 7;
     SegCursor cur{row0, range_lo, range_hi};
     int row, k0, k1, plo, phi;
@@ -514,8 +527,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           if (pt == 0) QMLA_TRS(4, s);
           if (pt == 0 && s == 0) QMLA_TR(0);
           if (ok) {
-            const uint32_t dst0 = kring + r.idx * kSlotBytes + ksc * 8192;
-            const int colb = FP8 ? s * 128 + kv * 16 : (s * 128 + ksc * 64 + kv * 8) * 2;
+            const uint32_t dst0 = kring + r.idx * kKSlotBytes + ksc * 8192;
+            const int colb = s * 256 + ksc * 128 + kv * 16;  // byte column of the row
             const int nbytes = max(0, min(16, a.qk_bytes - colb));  // zero past the QK width
             const uint64_t pol = s < NB ? pol_lat : pol_rope;
 #pragma unroll 4
@@ -547,7 +560,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const int nvw = a.use_tma ? 2 : 1;
     const int vw = warp == kWarpV ? nvw - 1 : 0;
     const int tpw = kTile / nvw;  // tokens per V warp
-    constexpr int kTokStep = 32 / kUnitsPerRow;  // tokens per warp-wide copy step
+    constexpr int kTokStep = 32 / kVUnits;  // tokens per warp-wide copy step
     SegCursor cur{row0, range_lo, range_hi};
     int row, k0, k1, plo, phi;
     uint32_t jt = 0;
@@ -570,13 +583,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           ok = mbar_wait(bar(b_vempty + r.idx), r.ph ^ 1, abort_flag, status);
           ok = __all_sync(0xffffffffu, ok);
           if (ok) {
-            const uint32_t dst0 = vring + r.idx * kSlotBytes;
-            const int u = lane % kUnitsPerRow, sc = u >> 3, v = u & 7;
+            const uint32_t dst0 = vring + r.idx * kVSlotBytes;
+            const int u = lane % kVUnits, sc = u >> 3, v = u & 7;
             const int colb = FP8 ? b * 128 + v * 16 : (b * 128 + sc * 64 + v * 8) * 2;
             const int steps = tpw / kTokStep;
 #pragma unroll 8
             for (int i = 0; i < steps; ++i) {
-              const int tl = i * kTokStep + lane / kUnitsPerRow;  // token within this warp's part
+              const int tl = i * kTokStep + lane / kVUnits;  // token within this warp's part
               const uint64_t src = __shfl_sync(0xffffffffu, i * kTokStep < 32 ? p0 : p1, tl & 31);
               const int t = vw * tpw + tl;
               cp_async_16_hint(dst0 + sc * 8192 + t * 128 + ((v ^ (t & 7)) << 4),
@@ -624,11 +637,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             if (qw == 0 && s == a.n_qk_slots - 1) QMLA_TR(4);
             fence_proxy_async_smem();  // cp.async writes -> tensor-core reads
             tc_fence_after();
-            const uint64_t ad0 = make_sdesc(kring + r.idx * kSlotBytes, 16, 1024, 2);
-            const uint64_t bd0 = q_desc0 + (uint64_t)(s * kSubs) * qc16;
+            const uint64_t ad0 = make_sdesc(kring + r.idx * kKSlotBytes, 16, 1024, 2);
+            const uint64_t bd0 = q_desc0 + (uint64_t)(s * kKSubs) * qc16;
 #pragma unroll
-            for (int sc = 0; sc < kSubs; ++sc) {
-              if (s * kSubs + sc < a.n_sub_qk) {
+            for (int sc = 0; sc < kKSubs; ++sc) {
+              if (s * kKSubs + sc < a.n_sub_qk) {
 #pragma unroll
                 for (int kk = 0; kk < 2; ++kk) {
                   const int ks = 2 * kk + qw;
@@ -698,7 +711,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             tc_fence_after();
             // A = V^T (M = 128 dims, K = tokens), MN-major, 128-byte swizzle:
             //   LBO = stride between 64-dim halves (bf16), SBO = 8-token group stride
-            const uint64_t ad0 = make_sdesc(vring + vidx * kSlotBytes, 8192, 1024, 2);
+            const uint64_t ad0 = make_sdesc(vring + vidx * kVSlotBytes, 8192, 1024, 2);
             const uint32_t d_o = tmem_base + col_o + b * OW;
 #pragma unroll
             for (int ks = 0; ks < kPvSteps; ++ks) {
@@ -1158,6 +1171,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   // ------------------------------------------------ teardown
   tc_fence_before();
   __syncthreads();
+#ifdef QMLA_TRACE
+  if (a.trace && threadIdx.x == 0) a.trace[6 * 4096 + blockIdx.x * 2 + 1] = globaltimer_ns();
+#endif
   if (warp == kWarpQK) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
