@@ -225,7 +225,18 @@ def run_ours(args) -> None:
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+        # NCCL announces its version on stdout while it initialises; the driver reads exactly one
+        # JSON line from stdout, so that banner goes to stderr
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=60))
+            dist.barrier()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
 
     from qwen_mla_vllm_b200.dcp import correct_attn_out, lse_all_gather, shard_lengths
     from qwen_mla_vllm_b200.mla_decode_attention import build_params, run_params
@@ -251,12 +262,16 @@ def run_ours(args) -> None:
             correct_attn_out(o, lses, rank)
             dist.all_reduce(o)
 
-    # clock ramp: ~1 s of untimed decode so the SM clock leaves its idle state, then W warm-up steps
+    # clock ramp: ~1 s of untimed local decode so the SM clock leaves its idle state (no
+    # collectives here: the loop is timed per rank, so its iteration count differs between
+    # ranks), then W warm-up steps that every rank takes the same number of times
     t_end = time.perf_counter() + 1.0
     while time.perf_counter() < t_end:
         for _ in range(5):
-            step()
+            run_params(params, dev)
         torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     for _ in range(args.warmup):
         step()
     sampler = ClockSampler(local).start()
