@@ -208,11 +208,9 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   const uint32_t rms_smem = (uint32_t)(2 * kTile * 16 * pl->rms_units);  // two staging buffers
   const uint32_t fixed = q_bytes + 2 * pl->p_bytes + misc_bytes + rms_smem + 1024 /*align slack*/;
   const int budget = std::min(di.max_smem, kMaxDynSmem) - (int)fixed;
-  // A PV issuer skips the other issuer's blocks of each tile, so it may wait on a
-  // V slot up to max(NB0, NB - NB0) positions after the last one it saw filled;
-  // one more slot than that keeps every parity wait within one phase.
-  const int nb0 = (nb + 1) / 2;
-  const int nv_min = std::max(nb0, nb - nb0) + 1;
+  // The single PV issuer takes V slots in ring order, so the loader is never more than
+  // one phase ahead of it; two slots let a load overlap the MMAs of the previous block.
+  const int nv_min = 2;
   if (budget < (int)(kslot + nv_min * vslot)) return QMLA_E_UNSUPPORTED;
   // K ring: the HBM stream (bandwidth x latency), ~55% of the rings; V ring: L2 re-reads for PV
   const int nk_max = (budget - nv_min * (int)vslot) / (int)kslot;

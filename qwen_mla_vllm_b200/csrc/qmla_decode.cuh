@@ -13,7 +13,9 @@
 //   warp  11    V loads: re-reads the tile's latent columns (L2-resident by then)
 //               into the V ring once QK of the tile has finished
 //   warps 12-13 QK issuers (tcgen05), one S partial each; warp 12 owns TMEM
-//   warps 14-15 PV issuers (tcgen05), about half of the 128-dim output blocks each
+//   warp  14    PV issuer (tcgen05), all 128-dim output blocks of a tile in order
+//               (two issuers interleaving blocks were 8% slower: the tensor pipe
+//               pays for every switch between accumulators); warp 15 is idle
 // Per 64-token tile:
 //   S^T[64 tok, heads] = K_tile . Q^T      tcgen05 M=64, K-major A and B
 //   softmax over tokens with the per-(token, head) rms divisor, base 2, lazy
@@ -301,7 +303,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t b_sfull = 2 * (nk + nv);        // [2] S ready (both QK issuers)
   const uint32_t b_sempty = b_sfull + 2;         // [2] S consumed
   const uint32_t b_pfull = b_sempty + 2;         // [2] P written (+ O rescaled)
-  const uint32_t b_odone = b_pfull + 2;          // [2] PV finished (both PV issuers)
+  const uint32_t b_odone = b_pfull + 2;          // [2] PV finished
   const uint32_t b_rfull = b_odone + 2;          // [2] rms tail staged
   const uint32_t b_rempty = b_rfull + 2;         // [2] rms staging consumed
   const uint32_t b_qfull = b_rempty + 2;         // [1] Q staged
@@ -331,7 +333,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       mbar_init(bar(b_sfull + i), KP);
       mbar_init(bar(b_sempty + i), kSoftmaxWarps);
       mbar_init(bar(b_pfull + i), kSoftmaxWarps);
-      mbar_init(bar(b_odone + i), 2);
+      mbar_init(bar(b_odone + i), 1);
       mbar_init(bar(b_rfull + i), a.use_tma ? 32 : kKThreads);
       mbar_init(bar(b_rempty + i), kSoftmaxWarps);
     }
@@ -675,13 +677,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp == kWarpPV || warp == kWarpPV + 1) {
-    // ====================================================== PV issuers
-    // Two warps, each owning about half of the 128-dim output blocks.
-    const int pw = warp - kWarpPV;
+  } else if (warp == kWarpPV) {
+    // ====================================================== PV issuer
     if (lane == 0) {
-      constexpr int NB0 = (NB + 1) / 2;
-      const int blk_lo = pw == 0 ? 0 : NB0, blk_hi = pw == 0 ? NB0 : NB;
       const uint32_t idesc = FP8 ? make_idesc_f16(0, 128, NPV, 1, 1)
                                  : make_idesc_f16(1, 128, NPV, 1, 1);
       SegCursor cur{row0, range_lo, range_hi};
@@ -693,7 +691,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         for (int k = k0; k < k1 && ok; ++k, ++jt) {
           const uint32_t pb = jt & 1;
           ok = mbar_wait(bar(b_pfull + pb), (jt >> 1) & 1, abort_flag, status);
-          if (pw == 0) QMLA_TR(7);
+          QMLA_TR(7);
           if (ok && k == k0 && sidx > 0)
             ok = mbar_wait(bar(b_ofree), (sidx - 1) & 1, abort_flag, status);
           // B = P^T (K = tokens, N = heads), MN-major, no swizzle: core matrix =
@@ -703,7 +701,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           for (int b = 0; b < NB; ++b) {
             const uint32_t vidx = rv.idx, vph = rv.ph;
             rv.next(nv);
-            if (!ok || b < blk_lo || b >= blk_hi) continue;
+            if (!ok) continue;
             ok = mbar_wait(bar(b_vfull + vidx), vph, abort_flag, status);
             if (!ok) continue;
             QMLA_TRS(3, 8 + b);
@@ -730,12 +728,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
           r = rv;
           if (ok) tc_commit(bar(b_odone + pb));
-          if (pw == 0) QMLA_TR(8);
+          QMLA_TR(8);
         }
         ++sidx;
       }
       if (jt > 0) {
-        const uint32_t fb = bar(b_fin + 2 + pw);
+        const uint32_t fb = bar(b_fin + 2);
         tc_commit(fb);
         volatile int never = 0;
         mbar_wait(fb, 0, &never, nullptr, 100000000ull);
