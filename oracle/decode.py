@@ -12,7 +12,7 @@ import numpy as np
 from .numerics import bf16_bits_to_f32, bf16_round, e4m3_decode, e4m3_encode, f32_to_bf16_bits, \
     log8_decode, log8_encode
 
-TILE = 64  # tokens per work unit of the sm_100a kernel's partition (this build's own plan)
+TILE = 128  # tokens per work unit of the sm_100a kernel's partition (this build's own plan)
 
 
 def _rms_values(rows: np.ndarray, heads: int, rms_offset: int, mode: str, kv_fp8: bool,

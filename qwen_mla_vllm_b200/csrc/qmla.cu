@@ -20,6 +20,7 @@ using namespace qmla;
 namespace {
 
 constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in limit per block on sm_100
+constexpr int kMaxRing = 8;          // K / V ring slots at most (bounds the barrier area)
 
 struct DevInfo {
   int sms = 0;
@@ -177,9 +178,9 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
     end = std::min<int64_t>(align_up(end, 16), p->kv_stride_token * es);
     pl->pf_bytes = (int)end;
   }
-  // K slots hold 256 bytes of each token's row (two 128-byte MMA sub-chunks)
-  pl->n_qk_slots = (pl->qk_bytes + 255) / 256;
+  // K slots hold one 128-byte column chunk of each of the tile's 128 tokens
   pl->n_sub_qk = (pl->qk_bytes + 127) / 128;
+  pl->n_qk_slots = pl->n_sub_qk;
   if (pl->n_sub_qk > kMaxQkChunks) return QMLA_E_UNSUPPORTED;
   // 16-byte vector loads of q rows (bf16 only; element strides in 2-byte units)
   auto vec_ok = [](const void* ptr, int64_t sr, int64_t sh) {
@@ -198,13 +199,13 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   pl->G = G;
 
   // shared memory map: K ring, V ring, Q, 2 P buffers, 2 rms staging buffers, misc
-  const uint32_t kslot = 16384u;              // 64 tokens x 256 bytes
+  const uint32_t kslot = 16384u;              // 128 tokens x 128 bytes
   const uint32_t vslot = fp8 ? 8192u : 16384u;  // 64 tokens x 128 dims
   const int q_rows = fp8 ? 2 * pl->nqk : pl->nqk;
   pl->q_chunk = (uint32_t)((q_rows + 7) / 8 * 1024);
   const uint32_t q_bytes = pl->q_chunk * pl->n_sub_qk;
-  pl->p_bytes = (uint32_t)(pl->npv * 128);
-  const uint32_t misc_bytes = 4096;
+  pl->p_bytes = (uint32_t)(pl->npv * 2 * kTile);  // P^T of a tile: bf16, or e4m3 hi + lo
+  const uint32_t misc_bytes = 5120;
   const uint32_t rms_smem = (uint32_t)(2 * kTile * 16 * pl->rms_units);  // two staging buffers
   const uint32_t fixed = q_bytes + 2 * pl->p_bytes + misc_bytes + rms_smem + 1024 /*align slack*/;
   const int budget = std::min(di.max_smem, kMaxDynSmem) - (int)fixed;
@@ -215,17 +216,19 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   // K ring: the HBM stream (bandwidth x latency), ~55% of the rings; V ring: L2 re-reads for PV
   const int nk_max = (budget - nv_min * (int)vslot) / (int)kslot;
   int nk = std::min(((budget * 11 / 20) + (int)kslot - 1) / (int)kslot, 3 * pl->n_qk_slots);
-  nk = std::max(1, std::min(nk, nk_max));
+  nk = std::max(1, std::min({nk, nk_max, kMaxRing}));
   // test hooks: QMLA_NK / QMLA_NV override the ring sizes (clamped to legal values)
-  if (const char* e = getenv("QMLA_NK")) nk = std::max(1, std::min(atoi(e), nk_max));
-  int nv = std::min((budget - nk * (int)kslot) / (int)vslot, 2 * nb);
+  if (const char* e = getenv("QMLA_NK")) nk = std::max(1, std::min({atoi(e), nk_max, kMaxRing}));
+  int nv = std::min({(budget - nk * (int)kslot) / (int)vslot, 2 * nb, kMaxRing});
   if (const char* e = getenv("QMLA_NV")) nv = std::min(atoi(e), nv);
   nv = std::max(nv, nv_min);
   if (nk * (int)kslot + nv * (int)vslot > budget) return QMLA_E_UNSUPPORTED;
   pl->nk = (uint32_t)nk;
   pl->nv = (uint32_t)nv;
+  // barriers, abort flag + TMEM slot, red[256] + hv[128] floats, tokptr[2][kTile]
   const uint32_t n_bars = 2 * (pl->nk + pl->nv) + 14 + kKdoneDepth + 4;
-  if ((n_bars * 8 + 15) / 16 * 16 + 16 + 1024 + 512 + 1024 > misc_bytes) return QMLA_E_UNSUPPORTED;
+  if ((n_bars * 8 + 15) / 16 * 16 + 16 + 1024 + 512 + 16 * kTile > misc_bytes)
+    return QMLA_E_UNSUPPORTED;
   uint32_t off = 0;
   pl->off_kring = off;
   off += pl->nk * kslot;

@@ -10,7 +10,7 @@
 
 namespace qmla {
 
-// Exclusive prefix of ceil(max(len,0)/64) over the rows, plus the total, and
+// Exclusive prefix of ceil(max(len,0)/kTile) over the rows, plus the total, and
 // clears the device status word.  One block of 1024 threads.
 // Partition rule shared with the host planner (qmla_plan).
 __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ seq_lens, int n,

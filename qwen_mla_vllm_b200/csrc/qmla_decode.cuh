@@ -1,32 +1,34 @@
 // Paged latent-KV MLA decode for B200 (sm_100a).
 //
-// One persistent CTA per SM walks a balanced, contiguous range of 64-token
+// One persistent CTA per SM walks a balanced, contiguous range of 128-token
 // tiles over all decode rows (rows are cut into segments at CTA boundaries and
 // merged afterwards).  Warp roles (16 warps, 512 threads):
-//   warps 0-7   softmax / epilogue.  Warp w reads TMEM sub-partition w%4 and
-//               owns half of the heads (w/4); two lanes per token, alternate
-//               heads (16x64b TMEM loads), so all 32 lanes are busy
-//   warps 8-10  K loads: 16-byte cp.async gathers of each tile's QK columns
-//               from the paged cache into the K ring (zero-filled past the
-//               attention width and past the row end), plus the tile's rms tail
-//               into a small staging buffer
-//   warp  11    V loads: re-reads the tile's latent columns (L2-resident by then)
-//               into the V ring once QK of the tile has finished
+//   warps 0-7   softmax / epilogue.  Warp w reads TMEM sub-partition w%4 (tokens
+//               32*(w%4) .. +31 of the tile, one token per lane) and owns half of
+//               the heads (w/4)
+//   warp  8     K loads: 3-D TMA boxes (128-byte column x a run of tokens of one
+//               page) into the K ring; warp 9 stages the rms tail.  Page sizes that
+//               are not multiples of 16 use 16-byte cp.async gathers from warps 8-10
+//   warps 10-11 V loads: re-read the tile's latent columns (L2-resident by then)
+//               into the V ring once QK of the tile has finished (warp 11 alone in
+//               cp.async mode)
 //   warps 12-13 QK issuers (tcgen05), one S partial each; warp 12 owns TMEM
 //   warp  14    PV issuer (tcgen05), all 128-dim output blocks of a tile in order
 //               (two issuers interleaving blocks were 8% slower: the tensor pipe
 //               pays for every switch between accumulators); warp 15 is idle
-// Per 64-token tile:
-//   S^T[64 tok, heads] = K_tile . Q^T      tcgen05 M=64, K-major A and B
+// Per 128-token tile:
+//   S^T[128 tok, heads] = K_tile . Q^T     tcgen05 M=128, K-major A and B
 //   softmax over tokens with the per-(token, head) rms divisor, base 2, lazy
 //   rescale (O is only rescaled when a running max grows by more than 2^8)
-//   O^T[rank, heads]  += V^T . P^T         tcgen05 M=128, MN-major A and B
-// K slots are freed as soon as their QK MMAs complete, so the HBM stream never
-// waits for the softmax.  bf16 caches use kind::f16.  FP8 caches use
-// kind::f8f6f4 on the raw e4m3 tile; q and P are each split into two e4m3 terms
-// (hi + lo): q's terms are stacked along N of the QK MMA (summed by the
-// softmax), P's terms are two PV MMAs into the same accumulator.  That keeps
-// ~bf16 precision without a dequantisation pass over the cache.
+//   O^T[rank, heads]   += V^T . P^T        tcgen05 M=128, MN-major A and B
+// The tile is 128 tokens because one tcgen05.mma costs about the same issue time
+// for M=64 and M=128 at these narrow N (24-48 heads): M=128 halves the QK MMAs per
+// token, which bounded the 64-token design.  K slots are freed as soon as their QK
+// MMAs complete, so the HBM stream never waits for the softmax.  bf16 caches use
+// kind::f16.  FP8 caches use kind::f8f6f4 on the raw e4m3 tile; q and P are each
+// split into two e4m3 terms (hi + lo): q's terms are stacked along N of the QK MMA
+// (summed by the softmax), P's terms are two PV MMAs into the same accumulator.
+// That keeps ~bf16 precision without a dequantisation pass over the cache.
 // Semantics follow the reference Triton kernel
 // qwen_mla/ops/mla_decode_attention.py:297-586 and its split merge :1064-1137.
 #pragma once
@@ -39,7 +41,7 @@
 
 namespace qmla {
 
-constexpr int kTile = 64;          // tokens per tile
+constexpr int kTile = 128;         // tokens per tile (the QK MMA's M)
 constexpr int kMaxQkChunks = 16;   // QK width <= 1024 elements
 constexpr int kMaxCtas = 160;      // persistent CTAs per launch (B200: 148 SMs)
 constexpr int kSoftmaxWarps = 8;
@@ -83,7 +85,7 @@ struct DecodeArgs {
   int num_rows, H, rank, qk_dim, rms_mode;
   int qk_bytes;     // bytes of a cache row the QK contraction reads
   int row_bytes;    // bytes of a cache row (kv_row_width * element size)
-  int n_qk_slots;   // K-ring slots loaded per tile (256 bytes of each token's row per slot)
+  int n_qk_slots;   // K-ring slots loaded per tile (one 128-byte column chunk per slot)
   int n_sub_qk;     // 128-byte-wide MMA sub-chunks of the QK width
   int rms_base_b;   // 16-byte-aligned first byte of the rms tail in a row
   int rms_units;    // 16-byte units staged per token (0: no rms); staging stride = 16 * rms_units
@@ -202,18 +204,19 @@ __device__ __forceinline__ void st_shared_u32(uint32_t a, uint32_t x) {
   asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(x) : "memory");
 }
 
-// Load N (2, 4, 6 or 8) 16x64b column pairs of one S block into v[0..N).
+// Load N (4, 8, 12 or 16) consecutive 32-bit columns of this thread's TMEM lane.
 template <int N>
-__device__ __forceinline__ void load_s_pairs(uint32_t taddr, float* v) {
-  if constexpr (N == 8) {
-    tmem_ld16x64<8>(taddr, v);
-  } else if constexpr (N == 6) {
-    tmem_ld16x64<4>(taddr, v);
-    tmem_ld16x64<2>(taddr + 8, v + 4);
-  } else if constexpr (N == 4) {
-    tmem_ld16x64<4>(taddr, v);
+__device__ __forceinline__ void load_cols(uint32_t taddr, float* v) {
+  if constexpr (N == 16) {
+    tmem_ld16(taddr, v);
+  } else if constexpr (N == 12) {
+    tmem_ld8(taddr, v);
+    tmem_ld4(taddr + 8, v + 8);
+  } else if constexpr (N == 8) {
+    tmem_ld8(taddr, v);
   } else {
-    tmem_ld16x64<2>(taddr, v);
+    static_assert(N == 4, "4, 8, 12 or 16 columns");
+    tmem_ld4(taddr, v);
   }
 }
 
@@ -228,7 +231,7 @@ struct Ring {
   }
 };
 
-// Cache-row address of token t (0..63) of tile k of a row; 0 past the row end
+// Cache-row address of token t (0..127) of tile k of a row; 0 past the row end
 // or for a page id outside the cache (those rows are zero-filled, never read).
 __device__ __forceinline__ uint64_t token_row_addr(const DecodeArgs& a, const int32_t* bt, int L,
                                                    int k, int t) {
@@ -246,13 +249,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     mla_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
   static_assert(NQK % 8 == 0 && NQK >= 8 && NQK <= 32, "heads rounded to 8..32");
   constexpr int NPV = NQK <= 16 ? 16 : 32;        // PV MMA N (multiple of 16)
-  // K ring slot: 64 tokens x 256 bytes of the row (128 bf16 / 256 e4m3 dims), two 128-byte
-  // swizzled sub-chunks.  V ring slot: 64 tokens x one 128-dim output block.
+  // QK MMA N: heads rounded up to 16 for bf16 (the extra B rows are read from the next Q
+  // chunk and only produce S columns nobody reads); the hi|lo q rows for FP8.
+  constexpr int NQKM = FP8 ? 2 * NQK : NPV;
+  // K ring slot: 128 tokens x one 128-byte column chunk of the row (64 bf16 / 128 e4m3
+  // dims), 128-byte swizzled.  V ring slot: 64 tokens x one 128-dim output block.
   constexpr int kKSlotBytes = 16384;
-  constexpr int kKSubs = 2;
-  constexpr int kKUnits = kKSubs * 8;             // 16-byte units per token per K slot
+  constexpr int kKUnits = 8;                      // 16-byte units per token per K slot
   constexpr int kVSlotBytes = FP8 ? 8192 : 16384;
   constexpr int kVUnits = (FP8 ? 1 : 2) * 8;      // 16-byte units per token per V slot
+  constexpr int kVTok = 64;                       // tokens per V slot (two per block and tile)
   constexpr int OW = NPV;                         // TMEM columns per O block
   constexpr int SWP = FP8 ? 2 * NPV : NPV;        // TMEM columns per S partial (hi|lo for FP8)
   constexpr int KP = 2;                           // S partials (one per QK issuer)
@@ -262,11 +268,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   constexpr uint32_t kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128
                                  : kCols <= 256 ? 256 : 512;
   static_assert(kCols <= 512, "TMEM budget");
-  constexpr int NJ = NQK / 4;   // heads per softmax thread
-  constexpr int NJP = NPV / 4;  // P^T columns per softmax thread (NJ real + zero padding)
+  constexpr int NJ = NQK / 2;   // heads per softmax thread (one token, half of the heads)
+  constexpr int NH = NPV / 2;   // P^T / O^T columns per head half (NJ real + zero padding)
   constexpr int kPvSteps = FP8 ? 2 : 4;  // K = 32 (e4m3) or 16 (bf16) tokens per PV MMA
   constexpr int kPvAStep = FP8 ? 4096 : 2048;
   constexpr int kPvBStep = (FP8 ? 4 : 2) * 16 * NPV;
+  constexpr int kPvHalfB = (kVTok / 8) * 16 * NPV;  // P^T bytes of one V slot's tokens
   constexpr int kKTokStep = kKThreads / kKUnits;  // tokens between a K thread's copies
   constexpr int kKIters = (kTile + kKTokStep - 1) / kKTokStep;
 
@@ -318,7 +325,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   float* red = reinterpret_cast<float*>(misc2 + 16);  // [2 halves][4 sp][32]
   float* hv = red + 256;                              // [4][32] per-head broadcast values
   // hv[0..31] alpha, hv[32..63] l, hv[64..95] m, hv[96..127] q scale (FP8)
-  uint64_t* tokptr = reinterpret_cast<uint64_t*>(hv + 128);  // [2][64] K-load row addresses
+  uint64_t* tokptr = reinterpret_cast<uint64_t*>(hv + 128);  // [2][128] K-load row addresses
 
   if (threadIdx.x == 0) {
     for (uint32_t i = 0; i < nk; ++i) {
@@ -359,20 +366,21 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t vring = sbase + a.off_vring;
   const uint32_t qbuf = sbase + a.off_q;
   const uint32_t pbuf = sbase + a.off_p;
-  const uint32_t rmsbuf = sbase + a.off_rms;  // [2][64 tokens][rstride]
+  const uint32_t rmsbuf = sbase + a.off_rms;  // [2][128 tokens][rstride]
   const int rstride = 16 * a.rms_units;       // rms staging bytes per token
   int* status = a.status;
 
   if (a.use_tma && warp == kWarpK) {
     // ====================================================== K loads by TMA
-    // Per 128-dim slot: one box per (128-byte column, run of tokens within a page);
-    // lanes issue the boxes of a slot side by side.  Columns past the QK width
-    // and pages outside the cache are zero-filled by the tensor map bounds.
+    // Per slot (one 128-byte column chunk of the tile): one box per run of tokens
+    // within a page; lanes issue the boxes of a slot side by side.  Columns past the
+    // QK width and pages outside the cache are zero-filled by the tensor map bounds.
     const uint64_t pol_lat = policy_evict_normal();
     const uint64_t pol_rope = policy_evict_first();
-    const int run = a.run_rows, nrun = kTile / run, nbox = kKSubs * nrun;
+    const int run = a.run_rows, nrun = kTile / run;
     const int xstep = FP8 ? 128 : 64;  // box width in elements
-    const int bsc = lane / nrun, bg = lane % nrun;  // this lane's box: sub-chunk, token run
+    const int lat_slots = a.rank * (FP8 ? 1 : 2) / 128;  // chunks the V loads read again
+    const int bg = lane;               // this lane's box: token run
     if (lane == 0) prefetch_tmap(&tmap);
     SegCursor cur{row0, range_lo, range_hi};
     int row, k0, k1, plo, phi;
@@ -390,7 +398,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       };
       int pg = run_page(k0);
       for (int k = k0; k < k1 && ok; ++k, ++jt) {
-        const int mypg = __shfl_sync(0xffffffffu, pg, bg);
+        const int mypg = pg;
         const int y = (k * kTile + bg * run) % a.page_size;
         int pg_next = -1;  // the next tile's page ids load while this tile's slots issue
         for (int s = 0; s < a.n_qk_slots && ok; ++s) {
@@ -403,10 +411,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
           ok = __shfl_sync(0xffffffffu, ok, 0);
           if (ok) {
-            if (lane < nbox)
-              tma_load_3d(kring + r.idx * kKSlotBytes + bsc * 8192 + bg * run * 128, &tmap,
-                          (kKSubs * s + bsc) * xstep, y, mypg, bar(b_kfull + r.idx),
-                          s < NB ? pol_lat : pol_rope);
+            if (lane < nrun)
+              tma_load_3d(kring + r.idx * kKSlotBytes + bg * run * 128, &tmap, s * xstep, y,
+                          mypg, bar(b_kfull + r.idx), s < lat_slots ? pol_lat : pol_rope);
             ++armed;
           }
           if (lane == 0) QMLA_TRS(1, s);
@@ -426,7 +433,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     __syncwarp();
   } else if (a.use_tma && warp == kWarpK + 1) {
     // ====================================================== rms tail + L2 prefetch (TMA mode)
-    // One warp; lane handles tokens `lane` and `lane + 32` of each tile.
+    // One warp; lane handles tokens lane + 32 * i (i < 4) of each tile.
     const uint64_t pol_lat = policy_evict_normal();
     const uint64_t pol_rope = policy_evict_first();
     SegCursor cur{row0, range_lo, range_hi};
@@ -438,14 +445,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       L = L < 0 ? 0 : L;
       const int32_t* bt = a.block_table + (int64_t)row * a.bt_stride;
       for (int kp = k0; kp < min(k1, k0 + kPrefetchTiles); ++kp) {  // no-op unless enabled
-        for (int h2 = 0; h2 < 2; ++h2) {
+        for (int h2 = 0; h2 < kTile / 32; ++h2) {
           const uint64_t pa = token_row_addr(a, bt, L, kp, lane + 32 * h2);
           if (pa) bulk_prefetch_l2(reinterpret_cast<const void*>(pa), a.pf_bytes, pol_lat);
         }
       }
       for (int k = k0; k < k1 && ok; ++k, ++jt) {
         if (kPrefetchTiles > 0 && k + kPrefetchTiles < k1) {
-          for (int h2 = 0; h2 < 2; ++h2) {
+          for (int h2 = 0; h2 < kTile / 32; ++h2) {
             const uint64_t pa = token_row_addr(a, bt, L, k + kPrefetchTiles, lane + 32 * h2);
             if (pa) bulk_prefetch_l2(reinterpret_cast<const void*>(pa), a.pf_bytes, pol_lat);
           }
@@ -455,7 +462,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           if (jt >= 2) ok = mbar_wait(bar(b_rempty + tb), ((jt - 2) >> 1) & 1, abort_flag, status);
           ok = __all_sync(0xffffffffu, ok);
           if (ok) {
-            for (int h2 = 0; h2 < 2; ++h2) {
+            for (int h2 = 0; h2 < kTile / 32; ++h2) {
               const int t = lane + 32 * h2;
               const uint64_t src = token_row_addr(a, bt, L, k, t);
               for (int u = 0; u < a.rms_units; ++u) {
@@ -477,9 +484,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const int pt = threadIdx.x - kWarpK * 32;  // 0..95
     const uint64_t pol_lat = policy_evict_normal();  // latent columns: read again for PV
     const uint64_t pol_rope = policy_evict_first();  // rope columns: read once
-    const int ku = pt % kKUnits;                     // this thread's 16-byte column unit
+    const int kv = pt % kKUnits;                     // this thread's 16-byte column unit
     const int kt0 = pt / kKUnits;                    // and first token
-    const int ksc = ku >> 3, kv = ku & 7;
+    const int lat_slots = a.rank * (FP8 ? 1 : 2) / 128;
+    // row addresses of tokens pt and pt + 96 of a tile (the tile's 128 tokens)
+    const int t1 = pt + kKThreads < kTile ? pt + kKThreads : -1;
     SegCursor cur{row0, range_lo, range_hi};
     int row, k0, k1, plo, phi;
     uint32_t jt = 0;
@@ -489,24 +498,33 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       int L = __ldg(a.seq_lens + row);
       L = L < 0 ? 0 : L;
       const int32_t* bt = a.block_table + (int64_t)row * a.bt_stride;
-      uint64_t nptr = pt < 64 ? token_row_addr(a, bt, L, k0, pt) : 0ull;
+      uint64_t nptr0 = token_row_addr(a, bt, L, k0, pt);
+      uint64_t nptr1 = t1 >= 0 ? token_row_addr(a, bt, L, k0, t1) : 0ull;
       // optional L2 prefetch kPrefetchTiles ahead of the loads (off by default)
-      if (pt < 64) {
-        for (int kp = k0; kp < min(k1, k0 + kPrefetchTiles); ++kp) {
-          const uint64_t pa = kp == k0 ? nptr : token_row_addr(a, bt, L, kp, pt);
+      for (int kp = k0; kp < min(k1, k0 + kPrefetchTiles); ++kp) {
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int t = h2 ? t1 : pt;
+          const uint64_t pa = t < 0 ? 0ull : token_row_addr(a, bt, L, kp, t);
           if (pa) bulk_prefetch_l2(reinterpret_cast<const void*>(pa), a.pf_bytes, pol_lat);
         }
       }
       for (int k = k0; k < k1 && ok; ++k, ++jt) {
         const uint32_t tb = jt & 1;
-        if (pt < 64) tokptr[tb * 64 + pt] = nptr;
+        tokptr[tb * kTile + pt] = nptr0;
+        if (t1 >= 0) tokptr[tb * kTile + t1] = nptr1;
         named_bar_sync(kBarK, kKThreads);
-        if (kPrefetchTiles > 0 && pt < 64 && k + kPrefetchTiles < k1) {
-          const uint64_t pa = token_row_addr(a, bt, L, k + kPrefetchTiles, pt);
-          if (pa) bulk_prefetch_l2(reinterpret_cast<const void*>(pa), a.pf_bytes, pol_lat);
+        if (kPrefetchTiles > 0 && k + kPrefetchTiles < k1) {
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int t = h2 ? t1 : pt;
+            const uint64_t pa = t < 0 ? 0ull : token_row_addr(a, bt, L, k + kPrefetchTiles, t);
+            if (pa) bulk_prefetch_l2(reinterpret_cast<const void*>(pa), a.pf_bytes, pol_lat);
+          }
         }
-        if (pt < 64 && k + 1 < k1) nptr = token_row_addr(a, bt, L, k + 1, pt);  // next tile
-        const uint64_t* tp = tokptr + tb * 64;
+        if (k + 1 < k1) {  // the next tile's row addresses
+          nptr0 = token_row_addr(a, bt, L, k + 1, pt);
+          if (t1 >= 0) nptr1 = token_row_addr(a, bt, L, k + 1, t1);
+        }
+        const uint64_t* tp = tokptr + tb * kTile;
         // ---- rms tail of the tile -> staging buffer tb
         if (a.rms_units > 0) {
           if (jt >= 2) ok = mbar_wait(bar(b_rempty + tb), ((jt - 2) >> 1) & 1, abort_flag, status);
@@ -523,16 +541,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             cp_async_mbar_arrive(bar(b_rfull + tb));
           }
         }
-        // ---- QK columns, one 128-dim slot at a time
+        // ---- QK columns, one 128-byte column chunk at a time
         for (int s = 0; s < a.n_qk_slots; ++s) {
           if (ok) ok = mbar_wait(bar(b_kempty + r.idx), r.ph ^ 1, abort_flag, status);
           if (pt == 0) QMLA_TRS(4, s);
           if (pt == 0 && s == 0) QMLA_TR(0);
           if (ok) {
-            const uint32_t dst0 = kring + r.idx * kKSlotBytes + ksc * 8192;
-            const int colb = s * 256 + ksc * 128 + kv * 16;  // byte column of the row
+            const uint32_t dst0 = kring + r.idx * kKSlotBytes;
+            const int colb = s * 128 + kv * 16;  // byte column of the row
             const int nbytes = max(0, min(16, a.qk_bytes - colb));  // zero past the QK width
-            const uint64_t pol = s < NB ? pol_lat : pol_rope;
+            const uint64_t pol = s < lat_slots ? pol_lat : pol_rope;
 #pragma unroll 4
             for (int i = 0; i < kKIters; ++i) {
               const int t = kt0 + i * kKTokStep;
@@ -561,7 +579,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const uint64_t pol = policy_evict_first();
     const int nvw = a.use_tma ? 2 : 1;
     const int vw = warp == kWarpV ? nvw - 1 : 0;
-    const int tpw = kTile / nvw;  // tokens per V warp
+    const int tpw = kVTok / nvw;  // tokens of each V slot per V warp
     constexpr int kTokStep = 32 / kVUnits;  // tokens per warp-wide copy step
     SegCursor cur{row0, range_lo, range_hi};
     int row, k0, k1, plo, phi;
@@ -573,15 +591,21 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       L = L < 0 ? 0 : L;
       const int32_t* bt = a.block_table + (int64_t)row * a.bt_stride;
       for (int k = k0; k < k1 && ok; ++k, ++jt) {
-        // this lane's tokens: vw*tpw + lane (and + 32 when one warp covers the tile)
-        const uint64_t p0 = token_row_addr(a, bt, L, k, vw * tpw + lane);
-        const uint64_t p1 = tpw > 32 ? token_row_addr(a, bt, L, k, vw * tpw + lane + 32) : 0ull;
+        // this lane's tokens of V slot half hh: hh*64 + vw*tpw + lane (and + 32 when one
+        // warp covers the slot)
+        uint64_t ph[2][2];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          ph[hh][0] = token_row_addr(a, bt, L, k, hh * kVTok + vw * tpw + lane);
+          ph[hh][1] = tpw > 32 ? token_row_addr(a, bt, L, k, hh * kVTok + vw * tpw + lane + 32) : 0ull;
+        }
         // the latent part is read again only after QK(jt) consumed it (it is in L2)
         ok = mbar_wait(bar(b_kdone + (jt % kKdoneDepth)), (jt / kKdoneDepth) & 1, abort_flag,
                        status);
         ok = __all_sync(0xffffffffu, ok);
         if (lane == 0 && vw == 0) QMLA_TR(6);
-        for (int b = 0; b < NB && ok; ++b) {
+        for (int bh = 0; bh < 2 * NB && ok; ++bh) {  // block bh/2, token half bh%2
+          const int b = bh >> 1, hh = bh & 1;
           ok = mbar_wait(bar(b_vempty + r.idx), r.ph ^ 1, abort_flag, status);
           ok = __all_sync(0xffffffffu, ok);
           if (ok) {
@@ -589,18 +613,19 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             const int u = lane % kVUnits, sc = u >> 3, v = u & 7;
             const int colb = FP8 ? b * 128 + v * 16 : (b * 128 + sc * 64 + v * 8) * 2;
             const int steps = tpw / kTokStep;
+            const uint64_t p0 = ph[hh][0], p1 = ph[hh][1];
 #pragma unroll 8
             for (int i = 0; i < steps; ++i) {
               const int tl = i * kTokStep + lane / kVUnits;  // token within this warp's part
               const uint64_t src = __shfl_sync(0xffffffffu, i * kTokStep < 32 ? p0 : p1, tl & 31);
-              const int t = vw * tpw + tl;
+              const int t = vw * tpw + tl;  // token within the V slot
               cp_async_16_hint(dst0 + sc * 8192 + t * 128 + ((v ^ (t & 7)) << 4),
                                src ? reinterpret_cast<const void*>(src + colb) : a.cache,
                                src ? 16u : 0u, pol);
             }
             cp_async_mbar_arrive(bar(b_vfull + r.idx));
           }
-          if (lane == 0 && vw == 0) QMLA_TRS(3, b);
+          if (lane == 0 && vw == 0 && bh < 16) QMLA_TRS(3, bh);
           r.next(nv);
         }
         if (lane == 0 && vw == 0) QMLA_TR(13);
@@ -609,13 +634,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (!ok) asm volatile("cp.async.wait_all;" ::: "memory");
   } else if (warp == kWarpQK || warp == kWarpQK + 1) {
     // ====================================================== QK issuers
-    // Each warp issues every other 16/32-wide K step of every sub-chunk into its
-    // own S partial (the softmax sums the partials): one thread issuing all
-    // MMAs of a tile is slower than the HBM stream.
+    // Each warp issues every other 16/32-wide K step of every column chunk into
+    // its own S partial (the softmax sums the partials): one thread issuing all
+    // MMAs of a tile was 10% slower overall.
     const int qw = warp - kWarpQK;
     if (lane == 0) {
-      const uint32_t idesc = FP8 ? make_idesc_f16(0, 64, 2 * NQK, 0, 0)
-                                 : make_idesc_f16(1, 64, NQK, 0, 0);
+      const uint32_t idesc = make_idesc_f16(FP8 ? 0 : 1, 128, NQKM, 0, 0);
       const uint32_t qc16 = a.q_chunk_bytes >> 4;              // Q chunk stride, descriptor units
       const uint64_t q_desc0 = make_sdesc(qbuf, 16, 1024, 2);  // Q chunk 0 (K-major, 128B swizzle)
       SegCursor cur{row0, range_lo, range_hi};
@@ -639,23 +663,18 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             if (qw == 0 && s == a.n_qk_slots - 1) QMLA_TR(4);
             fence_proxy_async_smem();  // cp.async writes -> tensor-core reads
             tc_fence_after();
+            // A = the slot (M = 128 tokens, K-major, 128-byte swizzle, 8-row groups 1 KB
+            // apart); B = Q chunk s (N rows, same layout).  K step = 32 bytes.
             const uint64_t ad0 = make_sdesc(kring + r.idx * kKSlotBytes, 16, 1024, 2);
-            const uint64_t bd0 = q_desc0 + (uint64_t)(s * kKSubs) * qc16;
+            const uint64_t bd0 = q_desc0 + (uint64_t)s * qc16;
 #pragma unroll
-            for (int sc = 0; sc < kKSubs; ++sc) {
-              if (s * kKSubs + sc < a.n_sub_qk) {
-#pragma unroll
-                for (int kk = 0; kk < 2; ++kk) {
-                  const int ks = 2 * kk + qw;
-                  const uint64_t ad = ad0 + (uint64_t)(sc * 512 + ks * 2);
-                  const uint64_t bd = bd0 + (uint64_t)(sc * qc16 + ks * 2);
-                  const uint32_t acc = (s == 0 && sc == 0 && kk == 0) ? 0u : 1u;
-                  if constexpr (FP8)
-                    tc_mma_f8_ss(d_s, ad, bd, idesc, acc);
-                  else
-                    tc_mma_f16_ss(d_s, ad, bd, idesc, acc);
-                }
-              }
+            for (int kk = 0; kk < 2; ++kk) {
+              const int ks = 2 * kk + qw;
+              const uint32_t acc = (s == 0 && kk == 0) ? 0u : 1u;
+              if constexpr (FP8)
+                tc_mma_f8_ss(d_s, ad0 + (uint64_t)(ks * 2), bd0 + (uint64_t)(ks * 2), idesc, acc);
+              else
+                tc_mma_f16_ss(d_s, ad0 + (uint64_t)(ks * 2), bd0 + (uint64_t)(ks * 2), idesc, acc);
             }
             if (qw == 0) QMLA_TRS(5, s);
             tc_commit(bar(b_kempty + r.idx));  // slot free once these MMAs complete
@@ -685,7 +704,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       SegCursor cur{row0, range_lo, range_hi};
       int row, k0, k1, plo, phi;
       uint32_t jt = 0, sidx = 0;
-      Ring r;  // V ring position of block 0 of the current tile
+      Ring r;  // V ring position (slots in order: block-major, then token half)
       bool ok = true;
       while (ok && next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi)) {
         for (int k = k0; k < k1 && ok; ++k, ++jt) {
@@ -697,14 +716,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           // B = P^T (K = tokens, N = heads), MN-major, no swizzle: core matrix =
           //   8 tokens x 16 bytes; LBO = token-group stride, SBO = head-block stride
           const uint64_t bd0 = make_sdesc(pbuf + pb * a.p_bytes, 16 * NPV, 128, 0);
-          Ring rv = r;
-          for (int b = 0; b < NB; ++b) {
-            const uint32_t vidx = rv.idx, vph = rv.ph;
-            rv.next(nv);
-            if (!ok) continue;
+          for (int bh = 0; bh < 2 * NB && ok; ++bh) {  // block bh/2, token half bh%2
+            const int b = bh >> 1, hh = bh & 1;
+            const uint32_t vidx = r.idx, vph = r.ph;
+            r.next(nv);
             ok = mbar_wait(bar(b_vfull + vidx), vph, abort_flag, status);
-            if (!ok) continue;
-            QMLA_TRS(3, 8 + b);
+            if (!ok) break;
             fence_proxy_async_smem();  // cp.async-written V slot -> tensor-core reads
             tc_fence_after();
             // A = V^T (M = 128 dims, K = tokens), MN-major, 128-byte swizzle:
@@ -714,8 +731,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
             for (int ks = 0; ks < kPvSteps; ++ks) {
               const uint64_t ad = ad0 + (uint64_t)(ks * (kPvAStep >> 4));
-              const uint64_t bd = bd0 + (uint64_t)(ks * (kPvBStep >> 4));
-              const uint32_t acc = (k == k0 && ks == 0) ? 0u : 1u;
+              const uint64_t bd = bd0 + (uint64_t)((hh * kPvHalfB + ks * kPvBStep) >> 4);
+              const uint32_t acc = (k == k0 && hh == 0 && ks == 0) ? 0u : 1u;
               if constexpr (FP8) {
                 // P = P_hi + P_lo: the lo half starts NPV/16 head blocks further on
                 tc_mma_f8_ss(d_o, ad, bd, idesc, acc);
@@ -726,7 +743,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             }
             tc_commit(bar(b_vempty + vidx));
           }
-          r = rv;
           if (ok) tc_commit(bar(b_odone + pb));
           QMLA_TR(8);
         }
@@ -747,21 +763,18 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const int tid = threadIdx.x;  // 0..255
     const int sp = warp & 3;      // TMEM sub-partition
     const int hw = warp >> 2;     // head half
-    const int cpar = (lane >> 1) & 1;
-    const int tt = sp * 16 + 8 * (lane & 1) + (lane >> 2);  // token of the tile
+    const int tt = sp * 32 + lane;  // token of the tile (TMEM lane of S)
     const int H = a.H;
     constexpr int nqk = NQK;
-    constexpr int nj = NJ;
     const uint32_t lane_base = (uint32_t)(sp * 32) << 16;
     int head[NJ];
 #pragma unroll
-    for (int j = 0; j < NJ; ++j) head[j] = hw * (nqk >> 1) + 2 * j + cpar;
-    // n-space (P^T / O^T column) of this thread's j-th head
-    auto ncol = [&](int j) { return hw * (NPV / 2) + cpar * (NPV / 4) + j; };
+    for (int j = 0; j < NJ; ++j) head[j] = hw * NJ + j;
+    // P^T / O^T column of head half hw, position j: hw * NH + j (j >= NJ is padding)
     auto head_of_n = [&](int n) -> int {
-      int h2 = n / (NPV / 2), c2 = (n % (NPV / 2)) / (NPV / 4), j2 = n % (NPV / 4);
-      if (j2 >= nj) return -1;
-      int h = h2 * (nqk >> 1) + 2 * j2 + c2;
+      const int j2 = n % NH;
+      if (j2 >= NJ) return -1;
+      const int h = (n / NH) * NJ + j2;
       return h < H ? h : -1;
     };
     const float kscale = (FP8 && a.k_scale) ? __ldg(a.k_scale) : 1.0f;
@@ -873,13 +886,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         if (tid == 0) QMLA_TR(9);
         if (ok) {
           tc_fence_after();
-          const uint32_t tb = tmem_base + lane_base + col_s + sb * SW + hw * (nqk >> 1);
+          const uint32_t tb = tmem_base + lane_base + col_s + sb * SW + hw * NJ;
           // S = sum of the KP partials (and of the hi / lo halves for FP8)
           float xp[KP * (FP8 ? 2 : 1)][NJ];
 #pragma unroll
           for (int p = 0; p < KP; ++p) {
-            load_s_pairs<NJ>(tb + p * SWP, xp[p * (FP8 ? 2 : 1)]);
-            if constexpr (FP8) load_s_pairs<NJ>(tb + p * SWP + nqk, xp[p * 2 + 1]);
+            load_cols<NJ>(tb + p * SWP, xp[p * (FP8 ? 2 : 1)]);
+            if constexpr (FP8) load_cols<NJ>(tb + p * SWP + nqk, xp[p * 2 + 1]);
           }
           tmem_wait_ld();
 #pragma unroll
@@ -951,29 +964,26 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         need = named_bar_or(kBarSoftmax, kSoftmaxThreads, need);
         if (tid == 0) QMLA_TR(11);
         if (need) {
-          // exact tile max per head: over this warp's 16 tokens, then the 4 sub-partitions
+          // exact tile max per head: over this warp's 32 tokens, then the 4 sub-partitions
           float wm[NJ];
 #pragma unroll
           for (int j = 0; j < NJ; ++j) {
             float v = x[j];
-            v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
-            v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
-            v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
-            v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
             wm[j] = v;
           }
-          if (lane < 4 && (lane & 1) == 0) {
+          if (lane == 0) {
 #pragma unroll
-            for (int j = 0; j < NJ; ++j) red[(hw * 4 + sp) * 32 + 2 * j + cpar] = wm[j];
+            for (int j = 0; j < NJ; ++j) red[(hw * 4 + sp) * 32 + j] = wm[j];
           }
           named_bar_sync(kBarSoftmax, kSoftmaxThreads);
           bool any_scale = false;
           float alpha[NJ];
 #pragma unroll
           for (int j = 0; j < NJ; ++j) {
-            const int c2 = 2 * j + cpar;
-            float t = fmaxf(fmaxf(red[(hw * 4 + 0) * 32 + c2], red[(hw * 4 + 1) * 32 + c2]),
-                            fmaxf(red[(hw * 4 + 2) * 32 + c2], red[(hw * 4 + 3) * 32 + c2]));
+            float t = fmaxf(fmaxf(red[(hw * 4 + 0) * 32 + j], red[(hw * 4 + 1) * 32 + j]),
+                            fmaxf(red[(hw * 4 + 2) * 32 + j], red[(hw * 4 + 3) * 32 + j]));
             float mn = fmaxf(m_ref[j], t);
             float al = (mn == -INFINITY) ? 1.f
                                          : (m_ref[j] == -INFINITY ? 0.f : exp2f(m_ref[j] - mn));
@@ -985,7 +995,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           any_scale = named_bar_or(kBarSoftmax, kSoftmaxThreads, any_scale);  // red[] free again
           if (any_scale) {
             // O holds tiles k0..k-1: wait for PV(k-1), then rescale it in TMEM
-            if (sp == 0 && lane < 4 && (lane & 1) == 0) {
+            if (sp == 0 && lane == 0) {
 #pragma unroll
               for (int j = 0; j < NJ; ++j) hv[head[j] & 31] = alpha[j];
             }
@@ -1022,9 +1032,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         // ---- P = 2^(x - m) -> P^T buffer pb
         {
-          float p[NJP];
+          float p[NH];
 #pragma unroll
-          for (int j = 0; j < NJP; ++j) {
+          for (int j = 0; j < NH; ++j) {
             if (j < NJ) {
               p[j] = (x[j] == -INFINITY) ? 0.f : ex2_approx(x[j] - m_ref[j]);
               l_part[j] += p[j];
@@ -1033,22 +1043,23 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             }
           }
           const uint32_t prow = pbuf + pb * a.p_bytes + (tt >> 3) * (16 * NPV) + (tt & 7) * 16;
-          const int n0 = ncol(0);
+          const int n0 = hw * NH;  // first P^T column of this head half (multiple of 8)
           if constexpr (!FP8) {
-            uint32_t w[NJP / 2];
+            // 8 heads (16 bytes) per core-matrix row; NH/8 core matrices 128 bytes apart
+            uint32_t w[NH / 2];
 #pragma unroll
-            for (int j = 0; j < NJP; j += 2)
+            for (int j = 0; j < NH; j += 2)
               w[j / 2] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(p[j])) |
                          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(p[j + 1])) << 16);
-            const uint32_t addr = prow + (n0 >> 3) * 128 + (n0 & 7) * 2;
-            if constexpr (NJP == 8)
-              st_shared_v4(addr, w[0], w[1], w[2], w[3]);
-            else
-              st_shared_v2(addr, w[0], w[1]);
-          } else {
-            uint32_t whi[NJP / 4], wlo[NJP / 4];
 #pragma unroll
-            for (int q4 = 0; q4 < NJP / 4; ++q4) {
+            for (int c = 0; c < NH / 8; ++c)
+              st_shared_v4(prow + ((n0 >> 3) + c) * 128, w[4 * c], w[4 * c + 1], w[4 * c + 2],
+                           w[4 * c + 3]);
+          } else {
+            // 16 heads (16 bytes) per core-matrix row; hi columns [0, NPV), lo [NPV, 2 NPV)
+            uint32_t whi[NH / 4], wlo[NH / 4];
+#pragma unroll
+            for (int q4 = 0; q4 < NH / 4; ++q4) {
               whi[q4] = 0u;
               wlo[q4] = 0u;
 #pragma unroll
@@ -1062,12 +1073,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             }
             const uint32_t ah = prow + (n0 >> 4) * 128 + (n0 & 15);
             const uint32_t al = prow + ((NPV + n0) >> 4) * 128 + ((NPV + n0) & 15);
-            if constexpr (NJP == 8) {
+            if constexpr (NH == 16) {
+              st_shared_v4(ah, whi[0], whi[1], whi[2], whi[3]);
+              st_shared_v4(al, wlo[0], wlo[1], wlo[2], wlo[3]);
+            } else {
               st_shared_v2(ah, whi[0], whi[1]);
               st_shared_v2(al, wlo[0], wlo[1]);
-            } else {
-              st_shared_u32(ah, whi[0]);
-              st_shared_u32(al, wlo[0]);
             }
           }
         }
@@ -1086,28 +1097,25 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
         for (int j = 0; j < NJ; ++j) {
           float v = l_part[j];
-          v += __shfl_xor_sync(0xffffffffu, v, 1);
-          v += __shfl_xor_sync(0xffffffffu, v, 4);
-          v += __shfl_xor_sync(0xffffffffu, v, 8);
-          v += __shfl_xor_sync(0xffffffffu, v, 16);
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
           ls[j] = v;
         }
-        if (lane < 4 && (lane & 1) == 0) {
+        if (lane == 0) {
 #pragma unroll
-          for (int j = 0; j < NJ; ++j) red[(hw * 4 + sp) * 32 + 2 * j + cpar] = ls[j];
+          for (int j = 0; j < NJ; ++j) red[(hw * 4 + sp) * 32 + j] = ls[j];
         }
         if (named_bar_or(kBarSoftmax, kSoftmaxThreads, !ok)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (sp == 0 && lane < 4 && (lane & 1) == 0) {
+        if (sp == 0 && lane == 0) {
 #pragma unroll
           for (int j = 0; j < NJ; ++j) {
-            const int c2 = 2 * j + cpar;
             if (head[j] < H) {
-              float lt = red[(hw * 4 + 0) * 32 + c2] + red[(hw * 4 + 1) * 32 + c2] +
-                         red[(hw * 4 + 2) * 32 + c2] + red[(hw * 4 + 3) * 32 + c2];
+              float lt = red[(hw * 4 + 0) * 32 + j] + red[(hw * 4 + 1) * 32 + j] +
+                         red[(hw * 4 + 2) * 32 + j] + red[(hw * 4 + 3) * 32 + j];
               hv[32 + head[j]] = lt;
               hv[64 + head[j]] = m_ref[j];
             }

@@ -218,7 +218,15 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-// 32 lanes x 32 bit, 8 / 16 / 32 consecutive columns per thread.
+// 32 lanes x 32 bit, 4 / 8 / 16 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, float* v) {
+  uint32_t r[4];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
+}
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
   uint32_t r[8];
   asm volatile(
@@ -238,30 +246,6 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const float* v) {
       : "memory");
 }
 
-// 16 lanes x 64 bit (half sub-partition): thread t reads lane base + 8*(t%2) + t/4,
-// 32-bit column 2*i + (t/2)%2 for i < N.
-template <int N>
-__device__ __forceinline__ void tmem_ld16x64(uint32_t taddr, float* v) {
-  uint32_t r[N];
-  if constexpr (N == 1) {
-    asm volatile("tcgen05.ld.sync.aligned.16x64b.x1.b32 {%0}, [%1];" : "=r"(r[0]) : "r"(taddr));
-  } else if constexpr (N == 2) {
-    asm volatile("tcgen05.ld.sync.aligned.16x64b.x2.b32 {%0,%1}, [%2];"
-                 : "=r"(r[0]), "=r"(r[1])
-                 : "r"(taddr));
-  } else if constexpr (N == 4) {
-    asm volatile("tcgen05.ld.sync.aligned.16x64b.x4.b32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(taddr));
-  } else if constexpr (N == 8) {
-    asm volatile("tcgen05.ld.sync.aligned.16x64b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
-                   "=r"(r[6]), "=r"(r[7])
-                 : "r"(taddr));
-  }
-#pragma unroll
-  for (int i = 0; i < N; ++i) v[i] = __uint_as_float(r[i]);
-}
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   uint32_t r[16];
   asm volatile(

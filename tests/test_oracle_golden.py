@@ -53,4 +53,4 @@ def test_rank_plan_arrays_exact():
     assert np.array_equal(kv_len, g["kv_len"])
     tp, indptr2, kv_len2 = oracle.plan_arrays(g["seq_lens"], int(g["page"]))
     assert np.array_equal(indptr2, g["kv_indptr"]) and np.array_equal(kv_len2, g["kv_len"])
-    assert tp[-1] == sum((int(L) + 63) // 64 for L in g["seq_lens"])
+    assert tp[-1] == sum((int(L) + oracle.TILE - 1) // oracle.TILE for L in g["seq_lens"])

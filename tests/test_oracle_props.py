@@ -112,6 +112,7 @@ def test_dcp_correct_special_values():
 
 def test_plan_arrays_edge_cases():
     tp, indptr, kv_len = oracle.plan_arrays(np.array([0, -5, 1, 64, 65, 128]), 16)
-    assert tp.tolist() == [0, 0, 0, 1, 2, 4, 6]
+    assert oracle.TILE == 128
+    assert tp.tolist() == [0, 0, 0, 1, 2, 3, 4]
     assert indptr.tolist() == [0, 0, 0, 1, 5, 10, 18]
     assert kv_len.tolist() == [0, 0, 1, 64, 65, 128]
