@@ -238,29 +238,54 @@ def run_ours(args) -> None:
             os.dup2(saved, 1)
             os.close(saved)
 
-    from qwen_mla_vllm_b200.dcp import correct_attn_out, lse_all_gather, shard_lengths
+    from qwen_mla_vllm_b200.dcp import P2PExchange, merge_across_ranks, shard_lengths
     from qwen_mla_vllm_b200.mla_decode_attention import build_params, run_params
 
     lens_all = seq_lens_cfg1()[:args.batch]
     lens = shard_lengths(lens_all, world, rank) if world > 1 else lens_all
     cache, q_h, bt_h, sl_h = make_inputs(lens, dev, seed=1000 + rank)
     q, bt, sl = q_h.to(dev), bt_h.to(dev), sl_h.to(dev)
-    o_dtype = torch.float32 if world > 1 else torch.bfloat16
     nb = len(lens_all)
-    o = torch.empty(nb, H, RANK, dtype=o_dtype, device=dev)
-    lse = torch.empty(nb, H, dtype=torch.float32, device=dev)
-    params = build_params(q, cache, o, lse, bt, sl, rank=RANK, qk_dim=QK, rms_offset=QK, rms_mode=1,
-                          page_size=PAGE, sm_scale=1 / 16)
+    merge_kind = args.dcp_merge if world > 1 else None
+    hs = H // world  # heads each rank keeps after the merge (vLLM's cp_lse_ag_out_rs layout)
+    ex = None
+    if merge_kind == "p2p":
+        # each rank decodes straight into slot (epoch & 1) of its exchange buffer; one kernel
+        # then merges the ranks' partials over NVLink peer memory
+        ex = P2PExchange(nb, H, RANK, device=dev)
+        slot_params = []
+        for s_epoch in (2, 1):  # slot 0, slot 1
+            o_s, l_s = ex.buf.partial(s_epoch)
+            slot_params.append(build_params(q, cache, o_s, l_s, bt, sl, rank=RANK, qk_dim=QK, rms_offset=QK,
+                                            rms_mode=1, page_size=PAGE, sm_scale=1 / 16))
+        o_m = torch.empty(nb, hs, RANK, dtype=torch.bfloat16, device=dev)
+        lse_m = torch.empty(nb, hs, dtype=torch.float32, device=dev)
+        params = slot_params[0]
+    else:
+        o = torch.empty(nb, H, RANK, dtype=torch.float32 if world > 1 else torch.bfloat16, device=dev)
+        lse = torch.empty(nb, H, dtype=torch.float32, device=dev)
+        params = build_params(q, cache, o, lse, bt, sl, rank=RANK, qk_dim=QK, rms_offset=QK, rms_mode=1,
+                              page_size=PAGE, sm_scale=1 / 16)
     run_params(params, dev)  # sizes and attaches the workspace once
     stream = torch.cuda.current_stream(dev)
-    launches_per_step = 3  # plan, decode, split merge
+    # our kernels per step: plan, decode, split merge (+ the P2P merge, or the NCCL path's correction)
+    launches_per_step = 3 + (1 if world > 1 else 0)
+
+    def decode():
+        if ex is not None:
+            run_params(slot_params[(ex.epoch + 1) & 1], dev)
+        else:
+            run_params(params, dev)
+
+    def merge():
+        if ex is not None:
+            ex.merge(out=o_m, lse_out=lse_m, mode="rs")
+        elif world > 1:
+            merge_across_ranks(o, lse, mode="rs")
 
     def step():
-        run_params(params, dev)
-        if world > 1:
-            lses = lse_all_gather(lse)
-            correct_attn_out(o, lses, rank)
-            dist.all_reduce(o)
+        decode()
+        merge()
 
     # clock ramp: ~1 s of untimed local decode so the SM clock leaves its idle state (no
     # collectives here: the loop is timed per rank, so its iteration count differs between
@@ -284,12 +309,9 @@ def run_ours(args) -> None:
     start.record(stream)
     for i in range(args.steps):
         ev[i][0].record(stream)
-        run_params(params, dev)
+        decode()
         ev[i][1].record(stream)
-        if world > 1:
-            lses = lse_all_gather(lse)
-            correct_attn_out(o, lses, rank)
-            dist.all_reduce(o)
+        merge()
     stop.record(stream)
     torch.cuda.synchronize()
     if world > 1:
@@ -318,23 +340,30 @@ def run_ours(args) -> None:
     # ---- end to end through the public entry point with host buffers (pinned) every step
     from qwen_mla_vllm_b200.mla_decode_attention import decode_attention_fwd
     q_pin, bt_pin, sl_pin = q_h.pin_memory(), bt_h.pin_memory(), sl_h.pin_memory()
-    o_host = torch.empty(nb, H, RANK, dtype=o_dtype).pin_memory()
-    lse_host = torch.empty(nb, H, dtype=torch.float32).pin_memory()
     logits = torch.empty(nb, H, 8, RANK + 1, dtype=torch.float32, device=dev)
     q_d, bt_d, sl_d = torch.empty_like(q), torch.empty_like(bt), torch.empty_like(sl)
+    res_o, res_lse = (o_m, lse_m) if ex is not None else (o, lse)
+    o_host = torch.empty(res_o.shape, dtype=res_o.dtype).pin_memory()
+    lse_host = torch.empty(res_lse.shape, dtype=torch.float32).pin_memory()
 
     def e2e_step():
         q_d.copy_(q_pin, non_blocking=True)
         bt_d.copy_(bt_pin, non_blocking=True)
         sl_d.copy_(sl_pin, non_blocking=True)
-        decode_attention_fwd(q_d, cache, cache[..., :RANK], o, lse, bt_d, sl_d, logits, 8, 1 / 16, PAGE,
+        o_w, l_w = ex.partial() if ex is not None else (o, lse)
+        decode_attention_fwd(q_d, cache, cache[..., :RANK], o_w, l_w, bt_d, sl_d, logits, 8, 1 / 16, PAGE,
                              is_mla=True, rms_offset=QK)
-        if world > 1:
-            lses = lse_all_gather(lse)
-            correct_attn_out(o, lses, rank)
-            dist.all_reduce(o)
-        o_host.copy_(o, non_blocking=True)
-        lse_host.copy_(lse, non_blocking=True)
+        if ex is not None:
+            ex.merge(out=o_m, lse_out=lse_m, mode="rs")
+            o_host.copy_(o_m, non_blocking=True)
+            lse_host.copy_(lse_m, non_blocking=True)
+        else:
+            if world > 1:
+                mo, ml = merge_across_ranks(o, lse, mode="rs")
+            else:
+                mo, ml = o, lse
+            o_host.copy_(mo, non_blocking=True)
+            lse_host.copy_(ml, non_blocking=True)
 
     for _ in range(max(3, args.warmup)):
         e2e_step()
@@ -354,7 +383,7 @@ def run_ours(args) -> None:
         e2e_ms = float(t[0])
     e2e_value = total_bytes / (e2e_ms / args.steps * 1e-3) / 1e12
     h2d = (q.numel() * q.element_size() + bt.numel() * 4 + sl.numel() * 4) * world
-    d2h = (o.numel() * o.element_size() + lse.numel() * 4) * world
+    d2h = (o_host.numel() * o_host.element_size() + lse_host.numel() * 4) * world
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -372,6 +401,10 @@ def run_ours(args) -> None:
                        "batch": nb, "heads": H, "rank": RANK, "rope": ROPE,
                        "rms": H, "row_bytes_read": ROW_READ, "page_size": PAGE, "sum_context": sum(lens_all),
                        "parallelism": f"dcp{world}" if world > 1 else "single",
+                       **({"dcp_merge": "one kernel over NVLink peer memory (qmla_dcp_p2p_merge), heads "
+                                        "scattered over ranks" if merge_kind == "p2p" else
+                           "NCCL all-gather lse + correction kernel + reduce-scatter over heads"}
+                          if world > 1 else {}),
                        "l2": "inputs larger than L2 (2.44 GB cache), no flush"},
             "seqs_per_s": nb / (step_ms * 1e-3),
             "hbm_frac_of_measured_peak": value * 1e3 / peak,
@@ -383,9 +416,11 @@ def run_ours(args) -> None:
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
-            "gpu_launches": launches_per_step * args.steps + (1 if world > 1 else 0) * args.steps,
+            "gpu_launches": launches_per_step * args.steps,
         }
         print(json.dumps(line), flush=True)
+    if ex is not None:
+        ex.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -399,6 +434,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--dcp-merge", choices=["p2p", "nccl"], default="p2p",
+                    help="N>1: merge the ranks' partials with one kernel over NVLink peer memory "
+                         "(default) or with NCCL (all-gather + correction + reduce-scatter)")
     ap.add_argument("--batch", type=int, default=B,
                     help="first N sequences of config1 (smaller cases for ncu captures; default: all 64)")
     args = ap.parse_args()

@@ -3,8 +3,9 @@
  *
  * C ABI of libqmla.so.  Plain pointers and sizes only; every device pointer is
  * a CUDA device address, `stream` is a cudaStream_t passed as void*.  No entry
- * point allocates device memory or synchronises the device (qmla_read_status
- * excepted), so the launching entry points may be recorded into a CUDA graph.
+ * point allocates device memory or synchronises the device (the qmla_dcp_buffer_*
+ * set-up calls and the two status readers excepted), so the launching entry
+ * points may be recorded into a CUDA graph.
  * Host-side the library keeps only per-device attributes and a small cache of
  * TMA descriptors.  Entry points return 0 on success or a negative QMLA_E_*
  * code.
@@ -27,6 +28,10 @@
  *                        fused into one merge of N (out, lse) partials.
  *   qmla_fp8_cache_write <- qwen_mla/mla_impl.py:309-342
  *                        (QwenMLATritonImpl.do_kv_cache_update, FP8 row writer).
+ *   qmla_dcp_p2p_merge <- the same cp_lse_ag_out_rs sequence (dcp_fix.py:133-142)
+ *                        done by one kernel over NVLink peer memory instead of
+ *                        NCCL; no counterpart in the reference, which refuses
+ *                        DCP (qwen_mla/mla_impl.py:552).
  */
 #ifndef QMLA_H_
 #define QMLA_H_
@@ -143,7 +148,7 @@ int qmla_read_status(const void* workspace, void* stream, int32_t* status);
 
 /* Host planner (no CUDA calls).  From host sequence lengths it writes, into
  * caller-owned host arrays:
- *   tile_prefix[num_rows+1]  exclusive prefix of ceil(len/64) (the decode
+ *   tile_prefix[num_rows+1]  exclusive prefix of ceil(len/128) (the decode
  *                            kernel's work partition; copy it to the device
  *                            and pass as plan_tile_prefix),
  *   kv_indptr[num_rows+1]    page-count prefix  (fi_decode.py:235-270),
@@ -184,6 +189,56 @@ int qmla_fp8_cache_write(const void* latent, int64_t latent_stride, const void* 
                          int32_t rank, int32_t rope, int32_t heads, int32_t rms_mode,
                          const float* k_scale, void* cache, int64_t cache_row_stride,
                          void* stream);
+
+/* ---- DCP over NVLink peer memory ------------------------------------------
+ * Each rank of a DCP group (one process per GPU) owns one exchange buffer:
+ *   [header 256 B: flags[8] u32 (epoch published by each rank), status u32]
+ *   [o partial, 2 slots of B*H*D f32, each 256-B aligned]
+ *   [lse partial, 2 slots of B*H f32 (natural log), each 256-B aligned]
+ * qmla_dcp_buffer_layout returns the byte offsets.  A decode step e writes the
+ * rank's partial into slot e&1 of its own buffer (qmla_mla_decode with o / lse
+ * pointing there, f32 o); qmla_dcp_p2p_merge(epoch = e) then merges all ranks'
+ * slot-e&1 partials, reading the peers' buffers through their IPC mappings.
+ * Epochs start at 1 and grow by one per step on every rank. */
+#define QMLA_DCP_MAX_WORLD 8
+#define QMLA_DCP_ALL_HEADS 0     /* every rank gets o[B, H, D] */
+#define QMLA_DCP_HEAD_SCATTER 1  /* rank r gets heads [r*H/world, (r+1)*H/world): o[B, H/world, D] */
+
+int qmla_dcp_buffer_layout(int32_t B, int32_t H, int32_t D, int64_t* total_bytes,
+                           int64_t* o_offset, int64_t* o_slot_bytes, int64_t* lse_offset,
+                           int64_t* lse_slot_bytes);
+/* cudaMalloc + zero-fill of an exchange buffer on `device`; writes its 64-byte
+ * CUDA IPC handle to ipc_handle.  Free with qmla_dcp_buffer_free. */
+int qmla_dcp_buffer_alloc(int32_t device, int64_t bytes, void** ptr, void* ipc_handle);
+/* Map a peer's exchange buffer (its IPC handle) on `device`; undo with
+ * qmla_dcp_buffer_close. */
+int qmla_dcp_buffer_open(int32_t device, const void* ipc_handle, void** ptr);
+int qmla_dcp_buffer_close(void* ptr);
+int qmla_dcp_buffer_free(void* ptr);
+
+typedef struct qmla_dcp_p2p_params {
+  void* bufs[QMLA_DCP_MAX_WORLD]; /* every rank's exchange buffer as mapped on this device */
+  int32_t world, rank;            /* 1 <= world <= 8 */
+  int32_t num_rows, num_heads, head_dim; /* head_dim % 4 == 0; H % world == 0 for scatter */
+  int32_t mode;                   /* QMLA_DCP_ALL_HEADS or QMLA_DCP_HEAD_SCATTER */
+  uint32_t epoch;                 /* this step's epoch (>= 1), equal on every rank */
+  void* out;                      /* [B, heads of this rank, D] */
+  int64_t out_stride_row, out_stride_head; /* elements */
+  int32_t out_dtype;              /* QMLA_DT_BF16 / F16 / F32 */
+  float* lse_out;                 /* [B, heads of this rank] natural log, contiguous; may be NULL */
+  int64_t timeout_ns;             /* bound on the wait for the peers' flags (<= 0: 2 s) */
+  int32_t device;
+} qmla_dcp_p2p_params;
+
+/* Publish this rank's epoch to every peer, wait (bounded) for theirs, merge:
+ *   o = sum_n exp(lse_n - lse_g) o_n,  lse_g = logsumexp_n lse_n
+ * (NaN / +inf partial LSEs count as -inf).  A wait that runs out sets the
+ * status word of this rank's buffer (qmla_dcp_read_status) and leaves `out`
+ * unwritten; the launch itself still succeeds. */
+int qmla_dcp_p2p_merge(const qmla_dcp_p2p_params* p, void* stream);
+/* Status word of an exchange buffer (0 = ok, 1 = a merge wait timed out);
+ * synchronises `stream`. */
+int qmla_dcp_read_status(const void* buffer, void* stream, int32_t* status);
 
 /* Human-readable text for a QMLA_E_* code. */
 const char* qmla_error_string(int code);

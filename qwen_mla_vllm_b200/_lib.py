@@ -82,6 +82,33 @@ class DecodeParams(ctypes.Structure):
     ]
 
 
+DCP_MAX_WORLD = 8
+DCP_ALL_HEADS, DCP_HEAD_SCATTER = 0, 1
+IPC_HANDLE_BYTES = 64
+
+
+class DcpP2PParams(ctypes.Structure):
+    """Mirror of ``qmla_dcp_p2p_params`` (field order and types must match qmla.h)."""
+
+    _fields_ = [
+        ("bufs", ctypes.c_void_p * DCP_MAX_WORLD),
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("num_rows", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("mode", ctypes.c_int32),
+        ("epoch", ctypes.c_uint32),
+        ("out", ctypes.c_void_p),
+        ("out_stride_row", ctypes.c_int64),
+        ("out_stride_head", ctypes.c_int64),
+        ("out_dtype", ctypes.c_int32),
+        ("lse_out", ctypes.c_void_p),
+        ("timeout_ns", ctypes.c_int64),
+        ("device", ctypes.c_int32),
+    ]
+
+
 # exported symbols and their ctypes prototypes: (restype, argtypes)
 _VP, _I32, _I64, _F32P = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p
 PROTOTYPES = {
@@ -97,6 +124,13 @@ PROTOTYPES = {
     "qmla_dcp_merge": (ctypes.c_int, [_VP, _I32, _VP, _VP, _I32, _VP, _I32, _I32, _I32, _I32, _VP]),
     "qmla_fp8_cache_write": (ctypes.c_int, [_VP, _I64, _VP, _I64, _VP, _I32, _I32, _I32, _I32, _I32, _VP,
                                             _VP, _I64, _VP]),
+    "qmla_dcp_buffer_layout": (ctypes.c_int, [_I32, _I32, _I32] + [ctypes.POINTER(_I64)] * 5),
+    "qmla_dcp_buffer_alloc": (ctypes.c_int, [_I32, _I64, ctypes.POINTER(_VP), _VP]),
+    "qmla_dcp_buffer_open": (ctypes.c_int, [_I32, _VP, ctypes.POINTER(_VP)]),
+    "qmla_dcp_buffer_close": (ctypes.c_int, [_VP]),
+    "qmla_dcp_buffer_free": (ctypes.c_int, [_VP]),
+    "qmla_dcp_p2p_merge": (ctypes.c_int, [ctypes.POINTER(DcpP2PParams), _VP]),
+    "qmla_dcp_read_status": (ctypes.c_int, [_VP, _VP, ctypes.POINTER(_I32)]),
 }
 
 _lib = None

@@ -13,6 +13,7 @@
 
 #include "qmla.h"
 #include "qmla_aux.cuh"
+#include "qmla_dcp.cuh"
 #include "qmla_decode.cuh"
 
 using namespace qmla;
@@ -338,7 +339,7 @@ extern "C" {
 void qmla_set_trace(void* dev_ptr) { g_trace = reinterpret_cast<unsigned long long*>(dev_ptr); }
 #endif
 
-int qmla_abi_version(void) { return 100; }
+int qmla_abi_version(void) { return 101; }
 
 const char* qmla_error_string(int code) {
   switch (code) {
@@ -550,6 +551,111 @@ int qmla_dcp_merge(const void* parts, int32_t parts_dtype, const float* part_lse
                                                reinterpret_cast<uint8_t*>(o), o_dtype, lse,
                                                n_parts, B, H, D);
   return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
+}
+
+int qmla_dcp_buffer_layout(int32_t B, int32_t H, int32_t D, int64_t* total_bytes,
+                           int64_t* o_offset, int64_t* o_slot_bytes, int64_t* lse_offset,
+                           int64_t* lse_slot_bytes) {
+  if (B < 0 || H <= 0 || D <= 0 || !total_bytes) return QMLA_E_INVALID;
+  const ExchangeLayout L = ExchangeLayout::make(B, H, D);
+  *total_bytes = L.total;
+  if (o_offset) *o_offset = kDcpHeader;
+  if (o_slot_bytes) *o_slot_bytes = L.o_slot;
+  if (lse_offset) *lse_offset = L.lse_off;
+  if (lse_slot_bytes) *lse_slot_bytes = L.lse_slot;
+  return QMLA_OK;
+}
+
+int qmla_dcp_buffer_alloc(int32_t device, int64_t bytes, void** ptr, void* ipc_handle) {
+  if (!ptr || !ipc_handle || bytes < kDcpHeader) return QMLA_E_INVALID;
+  *ptr = nullptr;
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess) return QMLA_E_CUDA;
+  if (cur != device && cudaSetDevice(device) != cudaSuccess) return QMLA_E_CUDA;
+  void* p = nullptr;
+  int rc = QMLA_OK;
+  if (cudaMalloc(&p, (size_t)bytes) != cudaSuccess) {
+    rc = QMLA_E_CUDA;
+  } else if (cudaMemset(p, 0, (size_t)bytes) != cudaSuccess ||
+             cudaDeviceSynchronize() != cudaSuccess ||
+             cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(ipc_handle), p) !=
+                 cudaSuccess) {
+    cudaFree(p);
+    p = nullptr;
+    rc = QMLA_E_CUDA;
+  }
+  *ptr = p;
+  if (cur != device) cudaSetDevice(cur);
+  return rc;
+}
+
+int qmla_dcp_buffer_open(int32_t device, const void* ipc_handle, void** ptr) {
+  if (!ptr || !ipc_handle) return QMLA_E_INVALID;
+  *ptr = nullptr;
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess) return QMLA_E_CUDA;
+  if (cur != device && cudaSetDevice(device) != cudaSuccess) return QMLA_E_CUDA;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (cur != device) cudaSetDevice(cur);
+  return e == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
+}
+
+int qmla_dcp_buffer_close(void* ptr) {
+  if (!ptr) return QMLA_E_INVALID;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
+}
+
+int qmla_dcp_buffer_free(void* ptr) {
+  if (!ptr) return QMLA_E_INVALID;
+  return cudaFree(ptr) == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
+}
+
+int qmla_dcp_p2p_merge(const qmla_dcp_p2p_params* p, void* stream) {
+  if (!p || p->world < 1 || p->world > kDcpMaxWorld || p->rank < 0 || p->rank >= p->world ||
+      p->num_rows < 0 || p->num_heads <= 0 || p->head_dim <= 0 || p->head_dim % 4 != 0 ||
+      !p->out || p->epoch == 0 || p->out_dtype < 0 || p->out_dtype > 2 ||
+      (p->mode != QMLA_DCP_ALL_HEADS && p->mode != QMLA_DCP_HEAD_SCATTER))
+    return QMLA_E_INVALID;
+  if (p->mode == QMLA_DCP_HEAD_SCATTER && p->num_heads % p->world != 0) return QMLA_E_INVALID;
+  for (int n = 0; n < p->world; ++n)
+    if (!p->bufs[n] || reinterpret_cast<uintptr_t>(p->bufs[n]) % 256 != 0) return QMLA_E_INVALID;
+  if (p->num_rows == 0) return QMLA_OK;
+  DevInfo di = dev_info(p->device);
+  if (!di.ok) return QMLA_E_CUDA;
+  P2PArgs a;
+  memset(&a, 0, sizeof(a));
+  for (int n = 0; n < p->world; ++n) a.bufs[n] = reinterpret_cast<uint8_t*>(p->bufs[n]);
+  a.world = p->world;
+  a.rank = p->rank;
+  a.B = p->num_rows;
+  a.H = p->num_heads;
+  a.D = p->head_dim;
+  a.mode = p->mode;
+  a.epoch = p->epoch;
+  a.out = reinterpret_cast<uint8_t*>(p->out);
+  a.out_sr = p->out_stride_row;
+  a.out_sh = p->out_stride_head;
+  a.out_dtype = p->out_dtype;
+  a.lse_out = p->lse_out;
+  a.timeout_ns = p->timeout_ns > 0 ? p->timeout_ns : 2000000000ll;
+  const int hs = p->mode == QMLA_DCP_HEAD_SCATTER ? p->num_heads / p->world : p->num_heads;
+  const int64_t items = (int64_t)p->num_rows * hs;
+  const int grid = (int)std::min<int64_t>(items, 4 * (int64_t)di.sms);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  dcp_p2p_merge_kernel<<<grid, 128, 0, st>>>(a);
+  return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
+}
+
+int qmla_dcp_read_status(const void* buffer, void* stream, int32_t* status) {
+  if (!buffer || !status) return QMLA_E_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const uint8_t* src = reinterpret_cast<const uint8_t*>(buffer) + 4 * kDcpMaxWorld;
+  if (cudaMemcpyAsync(status, src, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return QMLA_E_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return QMLA_E_CUDA;
+  return QMLA_OK;
 }
 
 int qmla_fp8_cache_write(const void* latent, int64_t latent_stride, const void* k_pe,

@@ -1,0 +1,141 @@
+// Decode-context-parallel merge over NVLink peer memory (sm_100a).
+//
+// Every rank of a DCP group owns one exchange buffer (ExchangeLayout below) that
+// the other ranks have mapped through CUDA IPC.  A decode step writes the rank's
+// partial (o, lse) for its KV shard into slot (epoch & 1) of its own buffer; the
+// merge kernel then
+//   1. publishes "epoch ready" into each peer's flag word for this rank (every
+//      block stores it, so no block depends on another block being resident),
+//   2. waits, bounded, until its own flag words show every peer at this epoch,
+//   3. reads the N partials of its (row, head) items straight from the peers'
+//      buffers and writes o = sum_n exp(lse_n - lse_g) o_n, lse_g = logsumexp lse_n
+//      (NaN / +inf partial LSEs count as -inf, as in dcp_fix.py:62-98).
+// Mode 1 gives rank r the heads [r*H/N, (r+1)*H/N) of every row (the layout of
+// vLLM's cp_lse_ag_out_rs, which qwen_mla/dcp_fix.py:133-142 patches); mode 0
+// gives every rank all heads.  One kernel replaces all-gather + correction +
+// reduce-scatter.  Two slots let step e+1's decode write while peers may still
+// read step e: a rank reaches step e+2's decode (slot e&1 again) only after its
+// merge e+1 saw every peer's epoch-(e+1) flag, which a peer stores only once its
+// merge e has finished reading.
+#pragma once
+#include <cuda_runtime.h>
+
+#include "qmla_decode.cuh"
+
+namespace qmla {
+
+constexpr int kDcpMaxWorld = 8;
+constexpr int kDcpHeader = 256;  // flags[kDcpMaxWorld] (u32), status (u32), padding
+
+// Byte offsets inside one rank's exchange buffer.
+struct ExchangeLayout {
+  int64_t o_slot, lse_off, lse_slot, total;
+  __host__ __device__ static ExchangeLayout make(int B, int H, int D) {
+    ExchangeLayout L;
+    L.o_slot = (((int64_t)B * H * D * 4) + 255) / 256 * 256;
+    L.lse_off = kDcpHeader + 2 * L.o_slot;
+    L.lse_slot = (((int64_t)B * H * 4) + 255) / 256 * 256;
+    L.total = L.lse_off + 2 * L.lse_slot;
+    return L;
+  }
+};
+
+struct P2PArgs {
+  uint8_t* bufs[kDcpMaxWorld];  // every rank's exchange buffer, mapped on this device
+  int world, rank, B, H, D, mode;
+  uint32_t epoch;
+  uint8_t* out;
+  int64_t out_sr, out_sh;
+  int out_dtype;
+  float* lse_out;  // [B][H or H/world], natural log; may be null
+  int64_t timeout_ns;
+};
+
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// grid: up to a few blocks per SM, 128 threads; items = B x (heads of this rank).
+__global__ void __launch_bounds__(128) dcp_p2p_merge_kernel(const P2PArgs a) {
+  __shared__ float w_s[kDcpMaxWorld];
+  __shared__ float lse_s;
+  __shared__ int fail_s;
+  const int tid = threadIdx.x;
+  const ExchangeLayout L = ExchangeLayout::make(a.B, a.H, a.D);
+  uint32_t* my_flags = reinterpret_cast<uint32_t*>(a.bufs[a.rank]);
+  // 1. publish: this rank's partial (written by the preceding decode on this stream) is complete
+  if (tid < a.world && tid != a.rank) {
+    __threadfence_system();
+    st_release_sys_u32(reinterpret_cast<uint32_t*>(a.bufs[tid]) + a.rank, a.epoch);
+  }
+  // 2. wait (bounded) for every peer's flag in this rank's own buffer
+  if (tid == 0) fail_s = 0;
+  __syncthreads();
+  if (tid < a.world && tid != a.rank) {
+    const uint64_t t0 = globaltimer_ns();
+    while ((int)(ld_acquire_sys_u32(my_flags + tid) - a.epoch) < 0) {
+      if (globaltimer_ns() - t0 > (uint64_t)a.timeout_ns) {
+        fail_s = 1;
+        atomicOr(reinterpret_cast<int*>(my_flags + kDcpMaxWorld), QMLA_DEV_ERR_TIMEOUT);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+  if (fail_s) return;
+  // 3. merge
+  const int hs = a.mode == 1 ? a.H / a.world : a.H;
+  const int h0 = a.mode == 1 ? a.rank * hs : 0;
+  const int slot = (int)(a.epoch & 1u);
+  const int osz = dt_size(a.out_dtype);
+  for (int item = blockIdx.x; item < a.B * hs; item += gridDim.x) {
+    const int b = item / hs, hl = item - b * hs, h = h0 + hl;
+    if (tid < 32) {
+      float v = -INFINITY;
+      if (tid < a.world) {
+        const float* lp = reinterpret_cast<const float*>(a.bufs[tid] + L.lse_off + slot * L.lse_slot);
+        v = lp[(int64_t)b * a.H + h];
+        if (v != v || v == INFINITY) v = -INFINITY;
+      }
+      float m = v;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const float e = (m == -INFINITY) ? 0.f : expf(v - m);
+      float s = e;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (tid < a.world) w_s[tid] = s > 0.f ? e / s : 0.f;
+      if (tid == 0) lse_s = s > 0.f ? m + logf(s) : -INFINITY;
+    }
+    __syncthreads();
+    const int64_t obase = ((int64_t)b * a.H + h) * a.D;
+    uint8_t* orow = a.out + ((int64_t)b * a.out_sr + (int64_t)hl * a.out_sh) * osz;
+    for (int d4 = tid; d4 < a.D / 4; d4 += blockDim.x) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int n = 0; n < a.world; ++n) {
+        const float w = w_s[n];
+        if (w == 0.f) continue;
+        const float4 v = *reinterpret_cast<const float4*>(
+            a.bufs[n] + kDcpHeader + slot * L.o_slot + (obase + 4 * d4) * 4);
+        acc.x += w * v.x;
+        acc.y += w * v.y;
+        acc.z += w * v.z;
+        acc.w += w * v.w;
+      }
+      store_from_float(orow + (4 * d4 + 0) * osz, a.out_dtype, acc.x);
+      store_from_float(orow + (4 * d4 + 1) * osz, a.out_dtype, acc.y);
+      store_from_float(orow + (4 * d4 + 2) * osz, a.out_dtype, acc.z);
+      store_from_float(orow + (4 * d4 + 3) * osz, a.out_dtype, acc.w);
+    }
+    if (tid == 0 && a.lse_out) a.lse_out[(int64_t)b * hs + hl] = lse_s;
+    __syncthreads();  // w_s / lse_s are rewritten by the next item
+  }
+}
+
+}  // namespace qmla

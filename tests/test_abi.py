@@ -38,27 +38,39 @@ def test_exports_every_declared_symbol(lib):
 
 
 def test_abi_version_and_errors(lib):
-    assert lib.qmla_abi_version() == 100
+    assert lib.qmla_abi_version() == 101
     for code, text in _lib.ERRORS.items():
         assert lib.qmla_error_string(code).decode() == text
     assert lib.qmla_error_string(0).decode() == "ok"
 
 
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
-def test_params_struct_layout_matches_header(tmp_path):
-    fields = [f for f, _ in _lib.DecodeParams._fields_]
+@pytest.mark.parametrize("cname,pystruct", [("qmla_decode_params", _lib.DecodeParams),
+                                            ("qmla_dcp_p2p_params", _lib.DcpP2PParams)])
+def test_params_struct_layout_matches_header(tmp_path, cname, pystruct):
+    fields = [f for f, _ in pystruct._fields_]
     src = ["#include <stdio.h>", "#include <stddef.h>", '#include "qmla.h"', "int main(void) {",
-           'printf("%zu\\n", sizeof(qmla_decode_params));']
-    src += [f'printf("%zu\\n", offsetof(qmla_decode_params, {f}));' for f in fields]
+           f'printf("%zu\\n", sizeof({cname}));']
+    src += [f'printf("%zu\\n", offsetof({cname}, {f}));' for f in fields]
     src += ["return 0; }"]
     c = tmp_path / "layout.c"
     c.write_text("\n".join(src))
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-I", str(HEADER.parent), str(c), "-o", str(exe)], check=True)
     vals = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
-    assert vals[0] == ctypes.sizeof(_lib.DecodeParams)
+    assert vals[0] == ctypes.sizeof(pystruct)
     for f, off in zip(fields, vals[1:]):
-        assert getattr(_lib.DecodeParams, f).offset == off, f
+        assert getattr(pystruct, f).offset == off, f
+
+
+def test_dcp_buffer_layout(lib):
+    vals = [ctypes.c_int64() for _ in range(5)]
+    assert lib.qmla_dcp_buffer_layout(64, 24, 768, *[ctypes.byref(v) for v in vals]) == 0
+    total, o_off, o_slot, lse_off, lse_slot = (v.value for v in vals)
+    assert o_off == 256 and o_slot == 64 * 24 * 768 * 4
+    assert lse_off == o_off + 2 * o_slot and lse_slot == 6144
+    assert total == lse_off + 2 * lse_slot
+    assert lib.qmla_dcp_buffer_layout(-1, 24, 768, *[ctypes.byref(v) for v in vals]) == -1
 
 
 def _plan(lib, lens, page):

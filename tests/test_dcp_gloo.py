@@ -1,12 +1,13 @@
-"""The DCP merge choreography (all-gather of lse, local correction, all-reduce of o) on two
-CPU ranks over gloo, with the oracle's correction in place of the CUDA kernel: the merged
-result of the two KV shards equals the single-rank decode."""
+"""The DCP merge choreography (all-gather of lse, local correction, then an all-reduce of o or
+a reduce-scatter over heads) on two CPU ranks over gloo, with the oracle's correction in place
+of the CUDA kernel: the merged result of the two KV shards equals the single-rank decode."""
 from __future__ import annotations
 
 import os
 import socket
 
 import numpy as np
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -59,25 +60,27 @@ def _oracle_correct(out, lses, cp_rank):
     return out, torch.from_numpy(g)
 
 
-def _worker(r, world, port, q_out):
+def _worker(r, world, port, q_out, mode="ar"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=r, world_size=world)
     try:
         from qwen_mla_vllm_b200.dcp import merge_across_ranks
         cache, bt, q, lens, kw = _case()
         o, lse = _shard_decode(cache, bt, q, lens, kw, world, r)
-        om, lm = merge_across_ranks(torch.from_numpy(o), torch.from_numpy(lse), correct=_oracle_correct)
+        om, lm = merge_across_ranks(torch.from_numpy(o), torch.from_numpy(lse), correct=_oracle_correct,
+                                    mode=mode)
         q_out.put((r, om.numpy(), lm.numpy()))
     finally:
         dist.destroy_process_group()
 
 
-def test_two_rank_merge_equals_full_decode():
+@pytest.mark.parametrize("mode", ["ar", "rs"])
+def test_two_rank_merge_equals_full_decode(mode):
     world = 2
     ctx = mp.get_context("spawn")
     q_out = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q_out)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q_out, mode)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q_out.get(timeout=120) for _ in range(world)]
@@ -86,9 +89,12 @@ def test_two_rank_merge_equals_full_decode():
         assert p.exitcode == 0
     cache, bt, q, lens, kw = _case()
     full_o, full_lse = oracle.decode(q, cache, bt, np.array(lens), **kw)
+    hs = q.shape[1] // world
     for r, om, lm in res:
-        assert np.abs(om - full_o).max() < 1e-10, r
-        assert np.abs(lm - full_lse).max() < 1e-10, r
+        h0, h1 = (r * hs, (r + 1) * hs) if mode == "rs" else (0, q.shape[1])
+        assert om.shape[1] == h1 - h0
+        assert np.abs(om - full_o[:, h0:h1]).max() < 1e-10, r
+        assert np.abs(lm - full_lse[:, h0:h1]).max() < 1e-10, r
 
 
 def test_shard_bounds_cover_sequence():

@@ -1,7 +1,8 @@
-"""Decode context parallelism on 2 GPUs over NCCL: each rank decodes its contiguous KV shard
-with the sm_100a kernel, the partials are merged (all-gather lse, correction kernel,
-all-reduce), and the result must equal the single-GPU decode of the whole sequences.
-Skipped when fewer than two GPUs are visible."""
+"""Decode context parallelism on 2 GPUs: each rank decodes its contiguous KV shard with the
+sm_100a kernel, the partials are merged, and the result must equal the single-GPU decode of
+the whole sequences.  Two merges: NCCL (all-gather lse, correction kernel, all-reduce) and
+the one-kernel merge over NVLink peer memory (qmla_dcp_p2p_merge, each rank keeping its half
+of the heads).  Skipped when fewer than two GPUs are visible."""
 from __future__ import annotations
 
 import os
@@ -31,7 +32,7 @@ def _case(device):
     return lens, make_bf16_case(len(lens), 24, 768, 232, 16, lens, seed=17, device=device)
 
 
-def _worker(rank, port, out_q):
+def _worker(rank, port, out_q, merge="nccl"):
     import datetime
     import sys
     sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
@@ -57,21 +58,36 @@ def _worker(rank, port, out_q):
             sls.append(max(hi - lo, 0))
         bt_s = torch.stack(bts)
         sl_s = torch.tensor(sls, dtype=torch.int32, device=dev)
-        o = torch.zeros(len(lens), 24, 768, dtype=torch.float32, device=dev)
-        lse = torch.zeros(len(lens), 24, dtype=torch.float32, device=dev)
+        ex = None
+        if merge == "p2p":
+            from qwen_mla_vllm_b200.dcp import P2PExchange
+            ex = P2PExchange(len(lens), 24, 768)
+            o, lse = ex.partial()
+        else:
+            o = torch.zeros(len(lens), 24, 768, dtype=torch.float32, device=dev)
+            lse = torch.zeros(len(lens), 24, dtype=torch.float32, device=dev)
         p = build_params(q, cache, o, lse, bt_s, sl_s, rank=768, qk_dim=1000, rms_offset=1000, rms_mode=1,
                          page_size=page, sm_scale=1 / 16)
         run_params(p, dev)
-        om, lm = merge_across_ranks(o, lse)
+        if ex is not None:
+            lm = torch.empty(len(lens), 24 // WORLD, dtype=torch.float32, device=dev)
+            om, _ = ex.merge(lse_out=lm, mode="rs", out_dtype=torch.float32)
+            h0, h1 = rank * (24 // WORLD), (rank + 1) * (24 // WORLD)
+        else:
+            om, lm = merge_across_ranks(o, lse)
+            h0, h1 = 0, 24
         torch.cuda.synchronize()
-        if rank == 0:
-            of = torch.zeros_like(o)
-            lf = torch.zeros_like(lse)
-            pf = build_params(q, cache, of, lf, bt, sl, rank=768, qk_dim=1000, rms_offset=1000, rms_mode=1,
-                              page_size=page, sm_scale=1 / 16)
-            run_params(pf, dev)
-            torch.cuda.synchronize()
-            out_q.put(((om - of).abs().max().item(), (lm - lf).abs().max().item()))
+        if ex is not None:
+            assert ex.status() == 0
+        of = torch.zeros(len(lens), 24, 768, dtype=torch.float32, device=dev)
+        lf = torch.zeros(len(lens), 24, dtype=torch.float32, device=dev)
+        pf = build_params(q, cache, of, lf, bt, sl, rank=768, qk_dim=1000, rms_offset=1000, rms_mode=1,
+                          page_size=page, sm_scale=1 / 16)
+        run_params(pf, dev)
+        torch.cuda.synchronize()
+        out_q.put((rank, (om - of[:, h0:h1]).abs().max().item(), (lm - lf[:, h0:h1]).abs().max().item()))
+        if ex is not None:
+            ex.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -79,16 +95,18 @@ def _worker(rank, port, out_q):
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD,
                     reason="needs 2 GPUs")
-def test_dcp_two_gpus_equals_single_gpu():
+@pytest.mark.parametrize("merge", ["nccl", "p2p"])
+def test_dcp_two_gpus_equals_single_gpu(merge):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, port, q)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, port, q, merge)) for r in range(WORLD)]
     for p in procs:
         p.start()
-    d_o, d_l = q.get(timeout=300)
+    res = [q.get(timeout=300) for _ in range(WORLD)]
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    assert d_o < 2e-3 and d_l < 1e-3, (d_o, d_l)
+    for rank, d_o, d_l in res:
+        assert d_o < 2e-3 and d_l < 1e-3, (merge, rank, d_o, d_l)
