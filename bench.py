@@ -342,9 +342,10 @@ def run_ours(args) -> None:
     q_pin, bt_pin, sl_pin = q_h.pin_memory(), bt_h.pin_memory(), sl_h.pin_memory()
     logits = torch.empty(nb, H, 8, RANK + 1, dtype=torch.float32, device=dev)
     q_d, bt_d, sl_d = torch.empty_like(q), torch.empty_like(bt), torch.empty_like(sl)
-    res_o, res_lse = (o_m, lse_m) if ex is not None else (o, lse)
-    o_host = torch.empty(res_o.shape, dtype=res_o.dtype).pin_memory()
-    lse_host = torch.empty(res_lse.shape, dtype=torch.float32).pin_memory()
+    # host copies of what a rank keeps: its H/N heads after a DCP merge, all heads on one GPU
+    heads_kept = hs if world > 1 else H
+    o_host = torch.empty(nb, heads_kept, RANK, dtype=o_m.dtype if ex is not None else o.dtype).pin_memory()
+    lse_host = torch.empty(nb, heads_kept, dtype=torch.float32).pin_memory()
 
     def e2e_step():
         q_d.copy_(q_pin, non_blocking=True)
