@@ -60,13 +60,18 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 using MapKey = std::tuple<const void*, int, int, int, int64_t, int64_t, int64_t, int>;
-std::map<MapKey, CUtensorMap> g_maps;
+std::map<MapKey, CacheMaps> g_maps;
 
-// 3-D map over the paged cache: (row element, token in page, page).  Each box is
-// one 128-byte column of `run` consecutive tokens of one page.  The row extent is
-// the QK width, so columns past it (rms tail, padding) are zero-filled, and so are
-// pages outside [0, num_pages).
-int cache_tensor_map(const qmla_decode_params* p, int run, CUtensorMap* out) {
+// The decode kernel's two maps over the paged cache (CacheMaps in qmla_decode.cuh):
+//   chunk: 3-D (row element, token in page, page), box = one 128-byte column x `run`
+//          tokens; the row extent is the QK width, so columns past it (rms tail,
+//          padding) are zero-filled;
+//   pair:  5-D (element of a 128-byte column, token in an 8-token group, column,
+//          8-token group in the page, page), box = two columns x `run` tokens, which
+//          lands as [8-token group][column][token][128 B]; the column extent counts the
+//          full columns only.
+// Pages outside [0, num_pages) are zero-filled by both.
+int cache_tensor_map(const qmla_decode_params* p, int run, CacheMaps* out) {
   const bool fp8 = p->kv_dtype == QMLA_DT_FP8E4M3;
   const int es = fp8 ? 1 : 2;
   MapKey key{p->kv_cache, p->kv_dtype, p->qk_dim, p->page_size, p->kv_num_pages,
@@ -82,17 +87,31 @@ int cache_tensor_map(const qmla_decode_params* p, int run, CUtensorMap* out) {
   auto fn = encode_fn();
   if (!fn) return QMLA_E_CUDA;
   CUtensorMapDataType dt = fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  cuuint64_t dims[3] = {(cuuint64_t)p->qk_dim, (cuuint64_t)p->page_size,
-                        (cuuint64_t)p->kv_num_pages};
-  cuuint64_t strides[2] = {(cuuint64_t)(p->kv_stride_token * es),
-                           (cuuint64_t)(p->kv_stride_page * es)};
-  cuuint32_t box[3] = {(cuuint32_t)(128 / es), (cuuint32_t)run, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUtensorMap m;
-  CUresult r = fn(&m, dt, 3, const_cast<void*>(p->kv_cache), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return QMLA_E_ALIGNMENT;
+  const int64_t tok_b = p->kv_stride_token * es, page_b = p->kv_stride_page * es;
+  CacheMaps m;
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)p->qk_dim, (cuuint64_t)p->page_size,
+                          (cuuint64_t)p->kv_num_pages};
+    cuuint64_t strides[2] = {(cuuint64_t)tok_b, (cuuint64_t)page_b};
+    cuuint32_t box[3] = {(cuuint32_t)(128 / es), (cuuint32_t)run, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(&m.chunk, dt, 3, const_cast<void*>(p->kv_cache), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return QMLA_E_ALIGNMENT;
+  }
+  {
+    const int full_chunks = p->qk_dim * es / 128;
+    cuuint64_t dims[5] = {(cuuint64_t)(128 / es), 8, (cuuint64_t)full_chunks,
+                          (cuuint64_t)(p->page_size / 8), (cuuint64_t)p->kv_num_pages};
+    cuuint64_t strides[4] = {(cuuint64_t)tok_b, 128, (cuuint64_t)(8 * tok_b), (cuuint64_t)page_b};
+    cuuint32_t box[5] = {(cuuint32_t)(128 / es), 8, 2, (cuuint32_t)(run / 8), 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = fn(&m.pair, dt, 5, const_cast<void*>(p->kv_cache), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return QMLA_E_ALIGNMENT;
+  }
   std::lock_guard<std::mutex> lk(g_mu);
   if (g_maps.size() > 4096) g_maps.clear();
   g_maps[key] = m;
@@ -114,7 +133,7 @@ int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 struct Plan {
   int npv, nb, nqk;
   int use_tma, run;
-  int n_qk_slots, n_sub_qk;
+  int n_qk_slots, n_sub_qk, n_full_chunks, cps, v_groups;
   int qk_bytes, row_bytes;
   int rms_bytes, rms_base_b, rms_units, rms_skip, pf_bytes;
   int G;
@@ -179,9 +198,18 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
     end = std::min<int64_t>(align_up(end, 16), p->kv_stride_token * es);
     pl->pf_bytes = (int)end;
   }
-  // K slots hold one 128-byte column chunk of each of the tile's 128 tokens
+  // K slots hold one or two 128-byte column chunks of each of the tile's 128 tokens.
+  // Two (paired layout, 4 KB TMA boxes) with three V groups measured fastest for the bf16
+  // rank-768 shape (config 1: 3.91 vs 3.74 TB/s); one chunk per slot with two V warps
+  // sharing each slot was faster for the smaller GLA head group (2.90 vs 2.46) and for
+  // FP8 (2.70 vs 2.63), so those keep it.
   pl->n_sub_qk = (pl->qk_bytes + 127) / 128;
-  pl->n_qk_slots = pl->n_sub_qk;
+  pl->n_full_chunks = pl->qk_bytes / 128;
+  bool paired = pl->use_tma && !fp8 && nb == 6;
+  if (getenv("QMLA_NO_PAIR")) paired = false;  // test hook: the one-column layout
+  pl->cps = paired ? 2 : 1;
+  pl->v_groups = paired ? 3 : 1;
+  pl->n_qk_slots = (pl->n_sub_qk + pl->cps - 1) / pl->cps;
   if (pl->n_sub_qk > kMaxQkChunks) return QMLA_E_UNSUPPORTED;
   // 16-byte vector loads of q rows (bf16 only; element strides in 2-byte units)
   auto vec_ok = [](const void* ptr, int64_t sr, int64_t sh) {
@@ -200,7 +228,7 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   pl->G = G;
 
   // shared memory map: K ring, V ring, Q, 2 P buffers, 2 rms staging buffers, misc
-  const uint32_t kslot = 16384u;              // 128 tokens x 128 bytes
+  const uint32_t kslot = 16384u * (uint32_t)pl->cps;  // 128 tokens x cps 128-byte columns
   const uint32_t vslot = fp8 ? 8192u : 16384u;  // 64 tokens x 128 dims
   const int q_rows = fp8 ? 2 * pl->nqk : pl->nqk;
   pl->q_chunk = (uint32_t)((q_rows + 7) / 8 * 1024);
@@ -210,13 +238,17 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   const uint32_t rms_smem = (uint32_t)(2 * kTile * 16 * pl->rms_units);  // two staging buffers
   const uint32_t fixed = q_bytes + 2 * pl->p_bytes + misc_bytes + rms_smem + 1024 /*align slack*/;
   const int budget = std::min(di.max_smem, kMaxDynSmem) - (int)fixed;
-  // The single PV issuer takes V slots in ring order, so the loader is never more than
-  // one phase ahead of it; two slots let a load overlap the MMAs of the previous block.
-  const int nv_min = 2;
+  // The V groups take the V slots in turn (slot n: group n % v_groups).  With at least as
+  // many slots as groups, a group's wait for slot n's position to be free comes after its
+  // own fill of slot n - v_groups, so the position is never two phases behind (a parity
+  // wait would then pass early; with fewer slots than groups calls hung until the 2 s
+  // wait limit).  Two slots at least, so a load overlaps the MMAs of the previous block.
+  const int nv_min = std::max(2, pl->v_groups);
   if (budget < (int)(kslot + nv_min * vslot)) return QMLA_E_UNSUPPORTED;
   // K ring: the HBM stream (bandwidth x latency), ~55% of the rings; V ring: L2 re-reads for PV
   const int nk_max = (budget - nv_min * (int)vslot) / (int)kslot;
   int nk = std::min(((budget * 11 / 20) + (int)kslot - 1) / (int)kslot, 3 * pl->n_qk_slots);
+  if (paired) nk = 2;  // 64 KB of K, the rest for V (swept: 2 x 32 KB + 5 x 16 KB best)
   nk = std::max(1, std::min({nk, nk_max, kMaxRing}));
   // test hooks: QMLA_NK / QMLA_NV override the ring sizes (clamped to legal values)
   if (const char* e = getenv("QMLA_NK")) nk = std::max(1, std::min({atoi(e), nk_max, kMaxRing}));
@@ -259,54 +291,59 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   return QMLA_OK;
 }
 
-template <bool FP8, int NB, int NQK>
-int launch_decode_t(const CUtensorMap& tmap, const DecodeArgs& a, uint32_t smem,
+template <bool FP8, int NB, int NQK, bool PAIR>
+int launch_decode_t(const CacheMaps& maps, const DecodeArgs& a, uint32_t smem,
                     cudaStream_t st) {
-  auto k = mla_decode_kernel<FP8, NB, NQK>;
+  auto k = mla_decode_kernel<FP8, NB, NQK, PAIR>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
     attr_err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
   });
   if (attr_err != cudaSuccess) return QMLA_E_CUDA;
-  k<<<a.G, kNumThreads, smem, st>>>(tmap, a);
+  k<<<a.G, kNumThreads, smem, st>>>(maps, a);
   return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
 }
 
-template <bool FP8, int NB>
-int launch_decode_nb(int nqk, const CUtensorMap& tmap, const DecodeArgs& a, uint32_t smem,
+template <bool FP8, int NB, bool PAIR>
+int launch_decode_nb(int nqk, const CacheMaps& maps, const DecodeArgs& a, uint32_t smem,
                      cudaStream_t st) {
   switch (nqk) {
     case 16:
-      return launch_decode_t<FP8, NB, 16>(tmap, a, smem, st);
+      return launch_decode_t<FP8, NB, 16, PAIR>(maps, a, smem, st);
     case 24:
-      return launch_decode_t<FP8, NB, 24>(tmap, a, smem, st);
+      return launch_decode_t<FP8, NB, 24, PAIR>(maps, a, smem, st);
     case 32:
-      return launch_decode_t<FP8, NB, 32>(tmap, a, smem, st);
+      return launch_decode_t<FP8, NB, 32, PAIR>(maps, a, smem, st);
   }
   return QMLA_E_UNSUPPORTED;
 }
 
 template <bool FP8>
-int launch_decode_fp(int nb, int nqk, const CUtensorMap& tmap, const DecodeArgs& a,
+int launch_decode_fp(int nb, int nqk, const CacheMaps& maps, const DecodeArgs& a,
                      uint32_t smem, cudaStream_t st) {
   switch (nb) {
     case 2:
-      return launch_decode_nb<FP8, 2>(nqk, tmap, a, smem, st);
+      return launch_decode_nb<FP8, 2, false>(nqk, maps, a, smem, st);
     case 3:
-      return launch_decode_nb<FP8, 3>(nqk, tmap, a, smem, st);
+      return launch_decode_nb<FP8, 3, false>(nqk, maps, a, smem, st);
     case 4:
-      return launch_decode_nb<FP8, 4>(nqk, tmap, a, smem, st);
+      return launch_decode_nb<FP8, 4, false>(nqk, maps, a, smem, st);
     case 6:
-      return launch_decode_nb<FP8, 6>(nqk, tmap, a, smem, st);
+      return launch_decode_nb<FP8, 6, false>(nqk, maps, a, smem, st);
   }
   return QMLA_E_UNSUPPORTED;
 }
 
-int launch_decode(bool fp8, int nb, int nqk, const CUtensorMap& tmap, const DecodeArgs& a,
-                  uint32_t smem, cudaStream_t st) {
-  return fp8 ? launch_decode_fp<true>(nb, nqk, tmap, a, smem, st)
-             : launch_decode_fp<false>(nb, nqk, tmap, a, smem, st);
+// paired K slots: instantiated for the bf16 rank-768 shape only (the planner's choice)
+int launch_decode(bool fp8, bool paired, int nb, int nqk, const CacheMaps& maps,
+                  const DecodeArgs& a, uint32_t smem, cudaStream_t st) {
+  if (paired) {
+    if (fp8 || nb != 6) return QMLA_E_UNSUPPORTED;
+    return launch_decode_nb<false, 6, true>(nqk, maps, a, smem, st);
+  }
+  return fp8 ? launch_decode_fp<true>(nb, nqk, maps, a, smem, st)
+             : launch_decode_fp<false>(nb, nqk, maps, a, smem, st);
 }
 
 #ifdef QMLA_TRACE
@@ -416,6 +453,8 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
   a.row_bytes = pl.row_bytes;
   a.n_qk_slots = pl.n_qk_slots;
   a.n_sub_qk = pl.n_sub_qk;
+  a.n_full_chunks = pl.n_full_chunks;
+
   a.rms_base_b = pl.rms_base_b;
   a.rms_units = pl.rms_units;
   a.rms_skip = pl.rms_skip;
@@ -454,10 +493,10 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
 #endif
 
   if (p->num_rows == 0) return QMLA_OK;
-  CUtensorMap tmap;
-  memset(&tmap, 0, sizeof(tmap));
+  CacheMaps maps;
+  memset(&maps, 0, sizeof(maps));
   if (pl.use_tma) {
-    rc = cache_tensor_map(p, pl.run, &tmap);
+    rc = cache_tensor_map(p, pl.run, &maps);
     if (rc != QMLA_OK) return rc;
   }
   if (!p->plan_tile_prefix) {
@@ -467,7 +506,8 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
     if (cudaMemsetAsync(a.status, 0, 4, st) != cudaSuccess) return QMLA_E_CUDA;
   }
   if (cudaGetLastError() != cudaSuccess) return QMLA_E_CUDA;
-  rc = launch_decode(p->kv_dtype == QMLA_DT_FP8E4M3, pl.nb, pl.nqk, tmap, a, pl.smem_total, st);
+  rc = launch_decode(p->kv_dtype == QMLA_DT_FP8E4M3, pl.cps == 2, pl.nb, pl.nqk, maps, a,
+                     pl.smem_total, st);
   if (rc != QMLA_OK) return rc;
   split_merge_kernel<<<dim3(p->num_rows, p->num_heads), 128, 0, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;

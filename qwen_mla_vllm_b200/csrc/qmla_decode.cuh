@@ -6,21 +6,30 @@
 //   warps 0-7   softmax / epilogue.  Warp w reads TMEM sub-partition w%4 (tokens
 //               32*(w%4) .. +31 of the tile, one token per lane) and owns half of
 //               the heads (w/4)
-//   warp  8     K loads: 3-D TMA boxes (128-byte column x a run of tokens of one
+//   warp  8     K loads: TMA boxes (two 128-byte columns x a run of tokens of one
 //               page) into the K ring; warp 9 stages the rms tail.  Page sizes that
 //               are not multiples of 16 use 16-byte cp.async gathers from warps 8-10
-//   warps 10-11 V loads: re-read the tile's latent columns (L2-resident by then)
-//               into the V ring once QK of the tile has finished (warp 11 alone in
-//               cp.async mode)
+//   warps 10, 11, 15  V loads: re-read the tile's latent columns (L2-resident by
+//               then) into the V ring once QK of the tile has finished (warps 11 and
+//               15 in cp.async mode), one whole V slot per warp in turn
 //   warps 12-13 QK issuers (tcgen05), one S partial each; warp 12 owns TMEM
 //   warp  14    PV issuer (tcgen05), all 128-dim output blocks of a tile in order
 //               (two issuers interleaving blocks were 8% slower: the tensor pipe
-//               pays for every switch between accumulators); warp 15 is idle
+//               pays for every switch between accumulators)
 // Per 128-token tile:
 //   S^T[128 tok, heads] = K_tile . Q^T     tcgen05 M=128, K-major A and B
 //   softmax over tokens with the per-(token, head) rms divisor, base 2, lazy
 //   rescale (O is only rescaled when a running max grows by more than 2^8)
 //   O^T[rank, heads]   += V^T . P^T        tcgen05 M=128, MN-major A and B
+// K ring slot: 128 tokens x two 128-byte column chunks (32 KB), laid out as
+// [8-token group][chunk][token in group][128 B], 128-byte swizzled.  Chunk c of a slot
+// is then a K-major SW128 MMA operand that starts at c * 1 KB with its 8-row groups
+// 2 KB apart, and one 5-D TMA box fills both chunks of a page run (4 KB for 16-token
+// pages).  TMA moves ~1.5x more bytes per SM with these boxes than with 2 KB boxes of
+// one column (probe: 46.9 vs 31.0 GB/s per SM), and 2 KB was the largest one-column
+// box a 16-token page allows.  A slot holding the row's partial last chunk is loaded
+// chunk by chunk through a 3-D map whose row extent zero-fills the columns past the
+// QK width, and keeps the plain layout (chunk c's 128 rows contiguous at c * 16 KB).
 // The tile is 128 tokens because one tcgen05.mma costs about the same issue time
 // for M=64 and M=128 at these narrow N (24-48 heads): M=128 halves the QK MMAs per
 // token, which bounded the 64-token design.  K slots are freed as soon as their QK
@@ -47,6 +56,7 @@ constexpr int kMaxCtas = 160;      // persistent CTAs per launch (B200: 148 SMs)
 constexpr int kSoftmaxWarps = 8;
 constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
 constexpr int kWarpK = 8, kNumKWarps = 3, kWarpV = 11, kWarpQK = 12, kWarpPV = 14;
+constexpr int kWarpVX = 15;  // the extra V-load warp
 constexpr int kNumWarps = 16, kNumThreads = kNumWarps * 32;
 constexpr int kKThreads = kNumKWarps * 32;
 constexpr int kRmsMaxUnits = 5;    // staged 16-byte units per token: <= 64 rms bytes + alignment
@@ -79,14 +89,15 @@ struct DecodeArgs {
   int64_t bt_stride;
   const int32_t* seq_lens;
   int page_size;
-  int use_tma;   // 1: K tiles by 3-D TMA boxes of run_rows tokens (page_size % 16 == 0)
-  int run_rows;  // tokens per TMA box: gcd(page_size, 64)
+  int use_tma;   // 1: K tiles by TMA boxes of run_rows tokens (page_size % 16 == 0)
+  int run_rows;  // tokens per TMA box: gcd(page_size, 128)
   // geometry
   int num_rows, H, rank, qk_dim, rms_mode;
   int qk_bytes;     // bytes of a cache row the QK contraction reads
   int row_bytes;    // bytes of a cache row (kv_row_width * element size)
-  int n_qk_slots;   // K-ring slots loaded per tile (one 128-byte column chunk per slot)
+  int n_qk_slots;   // K-ring slots loaded per tile (two 128-byte column chunks per slot)
   int n_sub_qk;     // 128-byte-wide MMA sub-chunks of the QK width
+  int n_full_chunks;  // chunks that lie entirely inside the QK width
   int rms_base_b;   // 16-byte-aligned first byte of the rms tail in a row
   int rms_units;    // 16-byte units staged per token (0: no rms); staging stride = 16 * rms_units
   int rms_skip;     // first rms byte within the staged units
@@ -243,19 +254,49 @@ __device__ __forceinline__ uint64_t token_row_addr(const DecodeArgs& a, const in
                                     (int64_t)(tok % a.page_size) * a.token_stride_b);
 }
 
+// Tensor maps over the paged cache (TMA mode).
+//   chunk: 3-D (row element, token in page, page); box = one 128-byte column x run tokens.
+//          Its row extent is the QK width, so columns past it are zero-filled.
+//   pair:  5-D (element of a 128-byte column, token in an 8-token group, column,
+//          8-token group in the page, page); box = two columns x run tokens, landing in
+//          the paired slot layout.  Its column extent counts only full columns.
+// Pages outside [0, num_pages) are zero-filled by both.
+struct CacheMaps {
+  CUtensorMap chunk;
+  CUtensorMap pair;
+};
+
+// With paired slots (PAIR), K slot s uses the plain layout (loaded column by column
+// through the 3-D map) when it holds a column that extends past the QK width (TMA mode);
+// otherwise the paired layout.  Without PAIR every slot holds one column, plain.
+template <bool PAIR>
+__device__ __forceinline__ bool slot_plain(const DecodeArgs& a, int s) {
+  if constexpr (!PAIR) {
+    return true;
+  } else {
+    const int last = min(2 * s + 1, a.n_sub_qk - 1);
+    return a.use_tma && last >= a.n_full_chunks;
+  }
+}
+
 // ---------------------------------------------------------------- the kernel
-template <bool FP8, int NB, int NQK>
+// PAIR: K slots of two columns (paired layout, 4 KB TMA boxes) and V slots filled by the
+// three V warps in turn; chosen for the bf16 rank-768 shape.  Otherwise one column per K
+// slot and two V warps sharing every V slot (see the planner for the measurements).
+template <bool FP8, int NB, int NQK, bool PAIR>
 __global__ void __launch_bounds__(kNumThreads, 1)
-    mla_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
+    mla_decode_kernel(const __grid_constant__ CacheMaps maps, const DecodeArgs a) {
   static_assert(NQK % 8 == 0 && NQK >= 8 && NQK <= 32, "heads rounded to 8..32");
   constexpr int NPV = NQK <= 16 ? 16 : 32;        // PV MMA N (multiple of 16)
   // QK MMA N: heads rounded up to 16 for bf16 (the extra B rows are read from the next Q
   // chunk and only produce S columns nobody reads); the hi|lo q rows for FP8.
   constexpr int NQKM = FP8 ? 2 * NQK : NPV;
-  // K ring slot: 128 tokens x one 128-byte column chunk of the row (64 bf16 / 128 e4m3
-  // dims), 128-byte swizzled.  V ring slot: 64 tokens x one 128-dim output block.
-  constexpr int kKSlotBytes = 16384;
-  constexpr int kKUnits = 8;                      // 16-byte units per token per K slot
+  // K ring slot: 128 tokens x two 128-byte column chunks of the row (the layout is in the
+  // file header).  V ring slot: 64 tokens x one 128-dim output block.
+  constexpr int kKChunkBytes = 16384;             // one column chunk of 128 tokens
+  constexpr int CPS = PAIR ? 2 : 1;               // column chunks per K slot
+  constexpr uint32_t kKSlotBytes = kKChunkBytes * CPS;
+  constexpr int VG = PAIR ? 3 : 1;                // V slot groups (see the V loader)
   constexpr int kVSlotBytes = FP8 ? 8192 : 16384;
   constexpr int kVUnits = (FP8 ? 1 : 2) * 8;      // 16-byte units per token per V slot
   constexpr int kVTok = 64;                       // tokens per V slot (two per block and tile)
@@ -274,8 +315,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   constexpr int kPvAStep = FP8 ? 4096 : 2048;
   constexpr int kPvBStep = (FP8 ? 4 : 2) * 16 * NPV;
   constexpr int kPvHalfB = (kVTok / 8) * 16 * NPV;  // P^T bytes of one V slot's tokens
-  constexpr int kKTokStep = kKThreads / kKUnits;  // tokens between a K thread's copies
-  constexpr int kKIters = (kTile + kKTokStep - 1) / kKTokStep;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -333,7 +372,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       mbar_init(bar(b_kempty + i), KP);
     }
     for (uint32_t i = 0; i < nv; ++i) {
-      mbar_init(bar(b_vfull + i), a.use_tma ? 64 : 32);  // V-load threads
+      mbar_init(bar(b_vfull + i), VG == 3 ? 32 : 64);  // the warps that fill a slot
       mbar_init(bar(b_vempty + i), 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -372,16 +411,18 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 
   if (a.use_tma && warp == kWarpK) {
     // ====================================================== K loads by TMA
-    // Per slot (one 128-byte column chunk of the tile): one box per run of tokens
-    // within a page; lanes issue the boxes of a slot side by side.  Columns past the
-    // QK width and pages outside the cache are zero-filled by the tensor map bounds.
+    // Per slot: one paired box per run of tokens within a page (both columns at once),
+    // or, for a slot with the partial last column, one 3-D box per (column, run); lanes
+    // issue the boxes of a slot side by side.
     const uint64_t pol_lat = policy_evict_normal();
     const uint64_t pol_rope = policy_evict_first();
     const int run = a.run_rows, nrun = kTile / run;
-    const int xstep = FP8 ? 128 : 64;  // box width in elements
-    const int lat_slots = a.rank * (FP8 ? 1 : 2) / 128;  // chunks the V loads read again
-    const int bg = lane;               // this lane's box: token run
-    if (lane == 0) prefetch_tmap(&tmap);
+    const int xstep = FP8 ? 128 : 64;  // column width in elements
+    const int lat_chunks = a.rank * (FP8 ? 1 : 2) / 128;  // columns the V loads read again
+    if (lane == 0) {
+      prefetch_tmap(&maps.chunk);
+      prefetch_tmap(&maps.pair);
+    }
     SegCursor cur{row0, range_lo, range_hi};
     int row, k0, k1, plo, phi;
     uint32_t jt = 0, armed = 0;
@@ -398,22 +439,37 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       };
       int pg = run_page(k0);
       for (int k = k0; k < k1 && ok; ++k, ++jt) {
-        const int mypg = pg;
+        // this lane's box in a plain slot: column lane / nrun, token run lane % nrun; in
+        // a paired slot: token run lane
+        const int bg = lane % nrun, bc = lane / nrun;
+        const int mypg = __shfl_sync(0xffffffffu, pg, bg);
         const int y = (k * kTile + bg * run) % a.page_size;
         int pg_next = -1;  // the next tile's page ids load while this tile's slots issue
         for (int s = 0; s < a.n_qk_slots && ok; ++s) {
           if (s == 0 && k + 1 < k1) pg_next = run_page(k + 1);
+          const bool plain = slot_plain<PAIR>(a, s);
+          const int c0 = CPS * s;  // first column chunk of the slot
+          const int nch = min(CPS, a.n_sub_qk - c0);
           if (lane == 0) {
             ok = mbar_wait(bar(b_kempty + r.idx), r.ph ^ 1, abort_flag, status);
-            if (ok) mbar_expect_tx(bar(b_kfull + r.idx), (uint32_t)kKSlotBytes);
+            if (ok)
+              mbar_expect_tx(bar(b_kfull + r.idx),
+                             plain ? (uint32_t)(nch * kKChunkBytes) : kKSlotBytes);
             QMLA_TRS(4, s);
             if (s == 0) QMLA_TR(0);
           }
           ok = __shfl_sync(0xffffffffu, ok, 0);
           if (ok) {
-            if (lane < nrun)
-              tma_load_3d(kring + r.idx * kKSlotBytes + bg * run * 128, &tmap, s * xstep, y,
-                          mypg, bar(b_kfull + r.idx), s < lat_slots ? pol_lat : pol_rope);
+            const uint32_t slot = kring + r.idx * kKSlotBytes;
+            if (plain) {
+              if (lane < nch * nrun)
+                tma_load_3d(slot + bc * kKChunkBytes + bg * run * 128, &maps.chunk,
+                            (c0 + bc) * xstep, y, mypg, bar(b_kfull + r.idx),
+                            c0 + bc < lat_chunks ? pol_lat : pol_rope);
+            } else if (lane < nrun) {
+              tma_load_5d(slot + lane * run * 256, &maps.pair, 0, 0, c0, y / 8, mypg,
+                          bar(b_kfull + r.idx), c0 < lat_chunks ? pol_lat : pol_rope);
+            }
             ++armed;
           }
           if (lane == 0) QMLA_TRS(1, s);
@@ -484,9 +540,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const int pt = threadIdx.x - kWarpK * 32;  // 0..95
     const uint64_t pol_lat = policy_evict_normal();  // latent columns: read again for PV
     const uint64_t pol_rope = policy_evict_first();  // rope columns: read once
-    const int kv = pt % kKUnits;                     // this thread's 16-byte column unit
-    const int kt0 = pt / kKUnits;                    // and first token
-    const int lat_slots = a.rank * (FP8 ? 1 : 2) / 128;
+    const int lat_chunks = a.rank * (FP8 ? 1 : 2) / 128;
     // row addresses of tokens pt and pt + 96 of a tile (the tile's 128 tokens)
     const int t1 = pt + kKThreads < kTile ? pt + kKThreads : -1;
     SegCursor cur{row0, range_lo, range_hi};
@@ -541,25 +595,30 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             cp_async_mbar_arrive(bar(b_rfull + tb));
           }
         }
-        // ---- QK columns, one 128-byte column chunk at a time
+        // ---- QK columns, two 128-byte column chunks per slot (paired layout); eight
+        // consecutive threads copy the 128 bytes of one (token, chunk)
         for (int s = 0; s < a.n_qk_slots; ++s) {
           if (ok) ok = mbar_wait(bar(b_kempty + r.idx), r.ph ^ 1, abort_flag, status);
           if (pt == 0) QMLA_TRS(4, s);
           if (pt == 0 && s == 0) QMLA_TR(0);
           if (ok) {
             const uint32_t dst0 = kring + r.idx * kKSlotBytes;
-            const int colb = s * 128 + kv * 16;  // byte column of the row
-            const int nbytes = max(0, min(16, a.qk_bytes - colb));  // zero past the QK width
-            const uint64_t pol = s < lat_slots ? pol_lat : pol_rope;
+            const int c0 = CPS * s;
+            const int nch = min(CPS, a.n_sub_qk - c0);
+            const bool plain = slot_plain<PAIR>(a, s);
+            const int upt = 8 * nch;  // 16-byte units per token in this slot
+            const uint64_t pol = c0 < lat_chunks ? pol_lat : pol_rope;
 #pragma unroll 4
-            for (int i = 0; i < kKIters; ++i) {
-              const int t = kt0 + i * kKTokStep;
-              if (t < kTile) {
-                const uint64_t src = tp[t];
-                const uint32_t nb = src ? (uint32_t)nbytes : 0u;
-                cp_async_16_hint(dst0 + t * 128 + ((kv ^ (t & 7)) << 4),
-                                 nb ? reinterpret_cast<const void*>(src + colb) : a.cache, nb, pol);
-              }
+            for (int q = pt; q < kTile * upt; q += kKThreads) {
+              const int t = q / upt, rem = q - t * upt, ci = rem >> 3, u = rem & 7;
+              const int colb = (c0 + ci) * 128 + u * 16;              // byte column of the row
+              const int nbytes = max(0, min(16, a.qk_bytes - colb));  // zero past the QK width
+              const uint64_t src = tp[t];
+              const uint32_t nb = src ? (uint32_t)nbytes : 0u;
+              const uint32_t row = plain ? dst0 + ci * kKChunkBytes + t * 128
+                                         : dst0 + (t >> 3) * 2048 + ci * 1024 + (t & 7) * 128;
+              cp_async_16_hint(row + ((u ^ (t & 7)) << 4),
+                               nb ? reinterpret_cast<const void*>(src + colb) : a.cache, nb, pol);
             }
             cp_async_mbar_arrive(bar(b_kfull + r.idx));
           }
@@ -572,40 +631,52 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
     }
     if (!ok) asm volatile("cp.async.wait_all;" ::: "memory");
-  } else if (warp == kWarpV || (a.use_tma && warp == kWarpK + 2)) {
+  } else if (warp == kWarpV || warp == kWarpVX || (a.use_tma && warp == kWarpK + 2)) {
     // ====================================================== V loads by cp.async (from L2)
-    // One warp (cp.async mode) or two (TMA mode, where warp 10 is free): warp vw of nvw
-    // gathers tokens [vw * 64/nvw, (vw + 1) * 64/nvw) of each latent block.
+    // V slot number n (counted over the CTA's whole run) is filled by group n % v_groups.
+    // v_groups == 3 (TMA mode): warps 10, 11 and 15 each fill whole slots in turn (more
+    // copies in flight; the config-1 shape gains).  v_groups == 1: warps 10 and 11 (TMA
+    // mode) or 11 and 15 (cp.async mode) split the 64 tokens of every slot (lower latency
+    // per slot; smaller heads/ranks gain).
     const uint64_t pol = policy_evict_first();
-    const int nvw = a.use_tma ? 2 : 1;
-    const int vw = warp == kWarpV ? nvw - 1 : 0;
-    const int tpw = kVTok / nvw;  // tokens of each V slot per V warp
+    constexpr int ngroups = VG;
+    const int vi = warp == kWarpV ? 0 : warp == kWarpVX ? 1 : 2;  // 11, 15, 10
+    constexpr int gw = VG == 3 ? 1 : 2;                            // warps per group
+    const int vg = VG == 3 ? vi : 0;                               // this warp's group
+    const int gi = VG == 3 ? 0 : (a.use_tma ? (warp == kWarpV ? 1 : 0) : vi);
+    const bool active = VG == 3 || (a.use_tma ? warp != kWarpVX : true);
+    constexpr int tpw = kVTok / gw;  // tokens of a V slot per warp of its group
     constexpr int kTokStep = 32 / kVUnits;  // tokens per warp-wide copy step
+    uint32_t vseq = 0;  // V slots seen so far
     SegCursor cur{row0, range_lo, range_hi};
     int row, k0, k1, plo, phi;
     uint32_t jt = 0;
     Ring r;
-    bool ok = true;
+    bool ok = active;
     while (ok && next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi)) {
       int L = __ldg(a.seq_lens + row);
       L = L < 0 ? 0 : L;
       const int32_t* bt = a.block_table + (int64_t)row * a.bt_stride;
       for (int k = k0; k < k1 && ok; ++k, ++jt) {
-        // this lane's tokens of V slot half hh: hh*64 + vw*tpw + lane (and + 32 when one
+        // this lane's tokens of V slot half hh: hh*64 + gi*tpw + lane (and + 32 when one
         // warp covers the slot)
         uint64_t ph[2][2];
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-          ph[hh][0] = token_row_addr(a, bt, L, k, hh * kVTok + vw * tpw + lane);
-          ph[hh][1] = tpw > 32 ? token_row_addr(a, bt, L, k, hh * kVTok + vw * tpw + lane + 32) : 0ull;
+          ph[hh][0] = token_row_addr(a, bt, L, k, hh * kVTok + gi * tpw + lane);
+          ph[hh][1] = tpw > 32 ? token_row_addr(a, bt, L, k, hh * kVTok + gi * tpw + lane + 32) : 0ull;
         }
         // the latent part is read again only after QK(jt) consumed it (it is in L2)
         ok = mbar_wait(bar(b_kdone + (jt % kKdoneDepth)), (jt / kKdoneDepth) & 1, abort_flag,
                        status);
         ok = __all_sync(0xffffffffu, ok);
-        if (lane == 0 && vw == 0) QMLA_TR(6);
-        for (int bh = 0; bh < 2 * NB && ok; ++bh) {  // block bh/2, token half bh%2
+        if (lane == 0 && vi == 0) QMLA_TR(6);
+        for (int bh = 0; bh < 2 * NB && ok; ++bh, ++vseq) {  // block bh/2, token half bh%2
           const int b = bh >> 1, hh = bh & 1;
+          if (ngroups > 1 && (int)(vseq % (uint32_t)ngroups) != vg) {  // another group's slot
+            r.next(nv);
+            continue;
+          }
           ok = mbar_wait(bar(b_vempty + r.idx), r.ph ^ 1, abort_flag, status);
           ok = __all_sync(0xffffffffu, ok);
           if (ok) {
@@ -618,17 +689,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             for (int i = 0; i < steps; ++i) {
               const int tl = i * kTokStep + lane / kVUnits;  // token within this warp's part
               const uint64_t src = __shfl_sync(0xffffffffu, i * kTokStep < 32 ? p0 : p1, tl & 31);
-              const int t = vw * tpw + tl;  // token within the V slot
+              const int t = gi * tpw + tl;  // token within the V slot
               cp_async_16_hint(dst0 + sc * 8192 + t * 128 + ((v ^ (t & 7)) << 4),
                                src ? reinterpret_cast<const void*>(src + colb) : a.cache,
                                src ? 16u : 0u, pol);
             }
             cp_async_mbar_arrive(bar(b_vfull + r.idx));
           }
-          if (lane == 0 && vw == 0 && bh < 16) QMLA_TRS(3, bh);
+          if (lane == 0 && bh < 16) QMLA_TRS(3, bh);
           r.next(nv);
         }
-        if (lane == 0 && vw == 0) QMLA_TR(13);
+        if (lane == 0 && vi == 0) QMLA_TR(13);
       }
     }
     if (!ok) asm volatile("cp.async.wait_all;" ::: "memory");
@@ -663,18 +734,30 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             if (qw == 0 && s == a.n_qk_slots - 1) QMLA_TR(4);
             fence_proxy_async_smem();  // cp.async writes -> tensor-core reads
             tc_fence_after();
-            // A = the slot (M = 128 tokens, K-major, 128-byte swizzle, 8-row groups 1 KB
-            // apart); B = Q chunk s (N rows, same layout).  K step = 32 bytes.
-            const uint64_t ad0 = make_sdesc(kring + r.idx * kKSlotBytes, 16, 1024, 2);
-            const uint64_t bd0 = q_desc0 + (uint64_t)s * qc16;
+            // A = column chunk ci of the slot (M = 128 tokens, K-major, 128-byte swizzle):
+            //   paired layout: starts at ci * 1 KB, 8-row groups 2 KB apart;
+            //   plain layout:  starts at ci * 16 KB, 8-row groups 1 KB apart.
+            // B = Q chunk 2s + ci (N rows, K-major SW128).  K step = 32 bytes.
+            const bool plain = slot_plain<PAIR>(a, s);
+            const int c0 = CPS * s;
+            const int nch = min(CPS, a.n_sub_qk - c0);
+            const uint32_t slot = kring + r.idx * kKSlotBytes;
 #pragma unroll
-            for (int kk = 0; kk < 2; ++kk) {
-              const int ks = 2 * kk + qw;
-              const uint32_t acc = (s == 0 && kk == 0) ? 0u : 1u;
-              if constexpr (FP8)
-                tc_mma_f8_ss(d_s, ad0 + (uint64_t)(ks * 2), bd0 + (uint64_t)(ks * 2), idesc, acc);
-              else
-                tc_mma_f16_ss(d_s, ad0 + (uint64_t)(ks * 2), bd0 + (uint64_t)(ks * 2), idesc, acc);
+            for (int ci = 0; ci < CPS; ++ci) {
+              if (ci < nch) {
+                const uint64_t ad0 = plain ? make_sdesc(slot + ci * kKChunkBytes, 16, 1024, 2)
+                                           : make_sdesc(slot + ci * 1024, 16, 2048, 2);
+                const uint64_t bd0 = q_desc0 + (uint64_t)(c0 + ci) * qc16;
+#pragma unroll
+                for (int kk = 0; kk < 2; ++kk) {
+                  const int ks = 2 * kk + qw;
+                  const uint32_t acc = (s == 0 && ci == 0 && kk == 0) ? 0u : 1u;
+                  if constexpr (FP8)
+                    tc_mma_f8_ss(d_s, ad0 + (uint64_t)(ks * 2), bd0 + (uint64_t)(ks * 2), idesc, acc);
+                  else
+                    tc_mma_f16_ss(d_s, ad0 + (uint64_t)(ks * 2), bd0 + (uint64_t)(ks * 2), idesc, acc);
+                }
+              }
             }
             if (qw == 0) QMLA_TRS(5, s);
             tc_commit(bar(b_kempty + r.idx));  // slot free once these MMAs complete

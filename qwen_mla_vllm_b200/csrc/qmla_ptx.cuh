@@ -102,6 +102,15 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int 
       "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(policy)
       : "memory");
 }
+// 5-D tiled tensor load (same completion and cache-policy semantics as tma_load_3d).
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const void* tmap, int c0, int c1, int c2,
+                                            int c3, int c4, uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;" ::"r"(dst),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(bar), "l"(policy)
+      : "memory");
+}
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
