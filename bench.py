@@ -337,44 +337,87 @@ def run_ours(args) -> None:
     traffic = profile_traffic() if world == 1 else None
     clocks = sampler.summary(t0, t1)
 
-    # ---- end to end through the public entry point with host buffers (pinned) every step
+    # ---- end to end through the public entry point with host buffers (pinned) every step.
+    # Every step copies its q / block table / lengths host->device and its (o, lse)
+    # device->host.  The copies run on a copy stream, double-buffered, so step i+1's inputs
+    # and step i-1's outputs move while step i decodes (as a serving loop would run them);
+    # the NCCL merge path keeps them serial.
     from qwen_mla_vllm_b200.mla_decode_attention import decode_attention_fwd
     q_pin, bt_pin, sl_pin = q_h.pin_memory(), bt_h.pin_memory(), sl_h.pin_memory()
     logits = torch.empty(nb, H, 8, RANK + 1, dtype=torch.float32, device=dev)
-    q_d, bt_d, sl_d = torch.empty_like(q), torch.empty_like(bt), torch.empty_like(sl)
-    # host copies of what a rank keeps: its H/N heads after a DCP merge, all heads on one GPU
-    heads_kept = hs if world > 1 else H
-    o_host = torch.empty(nb, heads_kept, RANK, dtype=o_m.dtype if ex is not None else o.dtype).pin_memory()
-    lse_host = torch.empty(nb, heads_kept, dtype=torch.float32).pin_memory()
+    heads_kept = hs if world > 1 else H  # a rank keeps its H/N heads after a DCP merge
+    out_dtype = o_m.dtype if ex is not None else o.dtype
+    pipelined = world == 1 or ex is not None
+    nbuf = 2 if pipelined else 1
+    ins = [(torch.empty_like(q), torch.empty_like(bt), torch.empty_like(sl)) for _ in range(nbuf)]
+    outs_dev = [(torch.empty(nb, heads_kept, RANK, dtype=out_dtype, device=dev),
+                 torch.empty(nb, heads_kept, dtype=torch.float32, device=dev)) for _ in range(nbuf)]
+    outs_host = [(torch.empty(nb, heads_kept, RANK, dtype=out_dtype).pin_memory(),
+                  torch.empty(nb, heads_kept, dtype=torch.float32).pin_memory()) for _ in range(nbuf)]
+    cs = torch.cuda.Stream(dev)
+    h2d_done = [torch.cuda.Event() for _ in range(nbuf)]
+    comp_done = [torch.cuda.Event() for _ in range(nbuf)]
 
-    def e2e_step():
-        q_d.copy_(q_pin, non_blocking=True)
-        bt_d.copy_(bt_pin, non_blocking=True)
-        sl_d.copy_(sl_pin, non_blocking=True)
-        o_w, l_w = ex.partial() if ex is not None else (o, lse)
+    def copy_in(b):
+        with torch.cuda.stream(cs):
+            for d, h in zip(ins[b], (q_pin, bt_pin, sl_pin)):
+                d.copy_(h, non_blocking=True)
+            h2d_done[b].record(cs)
+
+    def compute(b):
+        stream.wait_event(h2d_done[b])
+        q_d, bt_d, sl_d = ins[b]
+        if ex is not None:
+            o_w, l_w = ex.partial()
+        elif world == 1:
+            o_w, l_w = outs_dev[b]
+        else:
+            o_w, l_w = o, lse
         decode_attention_fwd(q_d, cache, cache[..., :RANK], o_w, l_w, bt_d, sl_d, logits, 8, 1 / 16, PAGE,
                              is_mla=True, rms_offset=QK)
         if ex is not None:
-            ex.merge(out=o_m, lse_out=lse_m, mode="rs")
-            o_host.copy_(o_m, non_blocking=True)
-            lse_host.copy_(lse_m, non_blocking=True)
+            ex.merge(out=outs_dev[b][0], lse_out=outs_dev[b][1], mode="rs")
+            res = outs_dev[b]
+        elif world > 1:
+            res = merge_across_ranks(o, lse, mode="rs")
         else:
-            if world > 1:
-                mo, ml = merge_across_ranks(o, lse, mode="rs")
-            else:
-                mo, ml = o, lse
-            o_host.copy_(mo, non_blocking=True)
-            lse_host.copy_(ml, non_blocking=True)
+            res = outs_dev[b]
+        comp_done[b].record(stream)
+        return res
 
-    for _ in range(max(3, args.warmup)):
-        e2e_step()
+    def copy_out(b, res):
+        with torch.cuda.stream(cs):
+            cs.wait_event(comp_done[b])
+            outs_host[b][0].copy_(res[0], non_blocking=True)
+            outs_host[b][1].copy_(res[1], non_blocking=True)
+
+    def run_e2e(n):
+        if not pipelined:
+            for i in range(n):
+                copy_in(0)
+                res = compute(0)
+                copy_out(0, res)
+            stream.wait_stream(cs)
+            return
+        copy_in(0)
+        if n > 1:
+            copy_in(1)
+        for i in range(n):
+            b = i % nbuf
+            res = compute(b)
+            copy_out(b, res)  # after compute(b): the copy stream waits for it
+            if i + nbuf < n:
+                copy_in(b)  # the next use of buffer b (after this step read its inputs)
+        stream.wait_stream(cs)
+
+    run_e2e(max(3, args.warmup))
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
+    cs.wait_event(e0)
+    run_e2e(args.steps)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
@@ -384,7 +427,7 @@ def run_ours(args) -> None:
         e2e_ms = float(t[0])
     e2e_value = total_bytes / (e2e_ms / args.steps * 1e-3) / 1e12
     h2d = (q.numel() * q.element_size() + bt.numel() * 4 + sl.numel() * 4) * world
-    d2h = (o_host.numel() * o_host.element_size() + lse_host.numel() * 4) * world
+    d2h = (outs_host[0][0].numel() * outs_host[0][0].element_size() + outs_host[0][1].numel() * 4) * world
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
