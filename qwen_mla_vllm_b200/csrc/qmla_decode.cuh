@@ -65,7 +65,8 @@ constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P may reach 2^8 before O is rescaled
 constexpr int kBarSoftmax = 1;             // named barrier id of the softmax warps
 constexpr int kBarK = 2;                   // named barrier id of the K-load warps
-constexpr int kKdoneDepth = 8;             // QK-done signals in flight (V loads trail QK)
+constexpr int kKdoneDepth = 8;
+constexpr int kEarlyQTiles = 16;           // segments this short stage the next Q early             // QK-done signals in flight (V loads trail QK)
 // Tiles of a row bulk-prefetched into L2 ahead of the K loads (TMA mode).  Off: the
 // prefetches share the bulk-copy engine with the K boxes and evicted the latent lines
 // that the V loads re-read (DRAM bytes per launch rose from 1.07x to 1.47x of the
@@ -196,6 +197,14 @@ __device__ __forceinline__ bool next_segment(const int32_t* prefix, SegCursor& c
   c.lo = end;
   ++c.row;
   return true;
+}
+
+// Row of the segment next_segment() would return next, or -1 (the cursor is not moved).
+__device__ __forceinline__ int peek_segment_row(const int32_t* prefix, const SegCursor& c) {
+  if (c.lo >= c.hi) return -1;
+  int r = c.row;
+  while (__ldg(prefix + r + 1) <= c.lo) ++r;
+  return r;
 }
 
 // Address of 16-byte unit u of row r in a 128-byte-swizzled block (1024-aligned base).
@@ -864,14 +873,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const bool cap = a.logit_cap > 0.f;
     const uint8_t* rms_smem = smem + a.off_rms;
     float m_ref[NJ], l_part[NJ], gs[NJ];
-    SegCursor cur{row0, range_lo, range_hi};
-    int row, k0, k1, plo, phi;
-    uint32_t jt = 0, sidx = 0;
-    bool ok = true;
-    while (ok && next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi)) {
-      int L = __ldg(a.seq_lens + row);
-      L = L < 0 ? 0 : L;
-      // ---------------- stage Q (the previous segment's QK is complete)
+    // Q of row qrow -> the Q buffer (bf16 rows, or e4m3 hi / lo rows with per-head scales in
+    // hv[96 + h] for FP8); all 256 softmax threads; arrives on qfull.
+    auto stage_q = [&](int qrow) {
       if constexpr (!FP8) {
         const int upr = a.n_sub_qk * 8;  // 16-byte units (8 elements) per head row
         for (int i = tid; i < nqk * upr; i += kSoftmaxThreads) {
@@ -879,8 +883,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           uint32_t w[4] = {0u, 0u, 0u, 0u};
           if (h < H && d0 < a.qk_dim) {
             const bool lat = d0 < a.rank;
-            const uint8_t* src = lat ? a.q + ((int64_t)row * a.q_sr + (int64_t)h * a.q_sh + d0) * 2
-                                     : a.q_pe + ((int64_t)row * a.qpe_sr + (int64_t)h * a.qpe_sh +
+            const uint8_t* src = lat ? a.q + ((int64_t)qrow * a.q_sr + (int64_t)h * a.q_sh + d0) * 2
+                                     : a.q_pe + ((int64_t)qrow * a.qpe_sr + (int64_t)h * a.qpe_sh +
                                                  (d0 - a.rank)) * 2;
             if ((lat ? a.q_vec : a.qpe_vec) && d0 + 8 <= a.qk_dim && a.q_dtype == 0) {
               uint4 v = __ldg(reinterpret_cast<const uint4*>(src));
@@ -908,8 +912,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           for (int d = lane; d < a.qk_dim; d += 32) {
             const uint8_t* src =
                 d < a.rank
-                    ? a.q + ((int64_t)row * a.q_sr + (int64_t)h * a.q_sh + d) * 2
-                    : a.q_pe + ((int64_t)row * a.qpe_sr + (int64_t)h * a.qpe_sh + (d - a.rank)) * 2;
+                    ? a.q + ((int64_t)qrow * a.q_sr + (int64_t)h * a.q_sh + d) * 2
+                    : a.q_pe + ((int64_t)qrow * a.qpe_sr + (int64_t)h * a.qpe_sh + (d - a.rank)) * 2;
             mx = fmaxf(mx, fabsf(load_as_float(src, a.q_dtype)));
           }
 #pragma unroll
@@ -931,8 +935,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
               uint8_t b = 0;
               if (d < a.qk_dim) {
                 const uint8_t* src =
-                    d < a.rank ? a.q + ((int64_t)row * a.q_sr + (int64_t)h * a.q_sh + d) * 2
-                               : a.q_pe + ((int64_t)row * a.qpe_sr + (int64_t)h * a.qpe_sh +
+                    d < a.rank ? a.q + ((int64_t)qrow * a.q_sr + (int64_t)h * a.q_sh + d) * 2
+                               : a.q_pe + ((int64_t)qrow * a.qpe_sr + (int64_t)h * a.qpe_sh +
                                            (d - a.rank)) * 2;
                 const float x = load_as_float(src, a.q_dtype) * sc;
                 const uint8_t hi = f32_to_e4m3(x);
@@ -947,6 +951,18 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       fence_proxy_async_smem();
       named_bar_sync(kBarSoftmax, kSoftmaxThreads);
       if (lane == 0) mbar_arrive(bar(b_qfull));
+    };
+    SegCursor cur{row0, range_lo, range_hi};
+    int row, k0, k1, plo, phi;
+    uint32_t jt = 0, sidx = 0;
+    bool ok = true;
+    // Q of the first segment; a later segment's Q is staged either before or after the
+    // previous segment's epilogue (see below).
+    bool have = next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi);
+    if (have) stage_q(row);
+    while (ok && have) {
+      int L = __ldg(a.seq_lens + row);
+      L = L < 0 ? 0 : L;
 #pragma unroll
       for (int j = 0; j < NJ; ++j) {
         m_ref[j] = -INFINITY;
@@ -1172,6 +1188,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
       if (!ok) break;
 
+      // ---------------- the next segment's Q, early after a short segment (its QK is
+      // complete): the next QK then overlaps this segment's PV tail and epilogue.  After a
+      // long segment the boundary costs little, and staging Q while the V loads stream
+      // measured 2% slower on config 1, so Q is staged after the epilogue there.
+      const bool early = k1 - k0 <= kEarlyQTiles;
+      if (early) {
+        const int nrow = peek_segment_row(a.tile_prefix, cur);
+        if (nrow >= 0) stage_q(nrow);
+      }
+
       // ---------------- epilogue: O^T / l -> output (or partial)
       {
         const uint32_t jl = jt - 1;
@@ -1255,6 +1281,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         if (lane == 0) mbar_arrive(bar(b_ofree));
       }
       ++sidx;
+      have = next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi);
+      if (have && !early) stage_q(row);
     }
   }
   // ------------------------------------------------ teardown
