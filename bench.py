@@ -43,8 +43,25 @@ WORKLOAD = ("config1: bf16 latent paged MLA decode, B=64, 1 query token, 24 head
             "row 768|232|24 bf16, L~U[1024,32768] (seed 1), 16-token pages in random order")
 
 
+# --workload cfg4 (BASELINE config 4 on the decode side: FP8 e4m3 cache with log8 rms codes,
+# batch 8 x 262,144 tokens, one query token) instead of the default config 1.  Not the headline
+# line: it measures the DCP scaling that BASELINE states at 262k context.
+FP8 = False
+WORKLOAD4 = ("config4: FP8-e4m3 latent paged MLA decode, B=8 x 262144 tokens, 1 query token, 24 heads, "
+             "row 768|232 e4m3 + 24 log8 rms codes, k_scale 0.01, 16-token pages in random order")
+
+
+def use_cfg4() -> None:
+    global FP8, B, ROW_READ, WORKLOAD
+    FP8, B = True, 8
+    ROW_READ = QK + H  # bytes of a row the decode reads: e4m3 latent + rope + one code per head
+    WORKLOAD = WORKLOAD4
+
+
 def seq_lens_cfg1() -> list[int]:
     import torch
+    if FP8:
+        return [262144] * B
     return torch.randint(1024, 32769, (B,), generator=torch.Generator().manual_seed(1)).tolist()
 
 
@@ -141,8 +158,14 @@ def make_inputs(lens: list[int], device, seed: int):
     pages = [(L + PAGE - 1) // PAGE for L in lens]
     P = max(1, sum(pages))
     gd = torch.Generator(device=device).manual_seed(seed)
-    cache = torch.randn(P, PAGE, 1, ROW, device=device, dtype=torch.bfloat16, generator=gd)
-    cache[..., QK:] = (torch.rand(P, PAGE, 1, ROW - QK, device=device, generator=gd) * 1.5 + 0.5).to(torch.bfloat16)
+    if FP8:  # e4m3 values of N(0,1) / k_scale, then one log8 rms code per head
+        cache = torch.randint(0, 256, (P, PAGE, 1, ROW), dtype=torch.uint8, device=device, generator=gd)
+        cache[..., :QK] = (torch.randn(P, PAGE, 1, QK, device=device, generator=gd) * 100).clamp(-448, 448) \
+            .to(torch.float8_e4m3fn).view(torch.uint8)
+        cache = cache.view(torch.float8_e4m3fn)
+    else:
+        cache = torch.randn(P, PAGE, 1, ROW, device=device, dtype=torch.bfloat16, generator=gd)
+        cache[..., QK:] = (torch.rand(P, PAGE, 1, ROW - QK, device=device, generator=gd) * 1.5 + 0.5).to(torch.bfloat16)
     perm = torch.randperm(P, generator=g)
     bt = torch.zeros(len(lens), max(1, max(pages)), dtype=torch.int32)
     off = 0
@@ -246,6 +269,9 @@ def run_ours(args) -> None:
     cache, q_h, bt_h, sl_h = make_inputs(lens, dev, seed=1000 + rank)
     q, bt, sl = q_h.to(dev), bt_h.to(dev), sl_h.to(dev)
     nb = len(lens_all)
+    ks = torch.tensor(0.01, dtype=torch.float32, device=dev) if FP8 else None
+    kw = dict(rank=RANK, qk_dim=QK, rms_offset=QK, rms_mode=3 if FP8 else 1, page_size=PAGE, sm_scale=1 / 16,
+              k_scale=ks)
     merge_kind = args.dcp_merge if world > 1 else None
     hs = H // world  # heads each rank keeps after the merge (vLLM's cp_lse_ag_out_rs layout)
     ex = None
@@ -256,16 +282,14 @@ def run_ours(args) -> None:
         slot_params = []
         for s_epoch in (2, 1):  # slot 0, slot 1
             o_s, l_s = ex.buf.partial(s_epoch)
-            slot_params.append(build_params(q, cache, o_s, l_s, bt, sl, rank=RANK, qk_dim=QK, rms_offset=QK,
-                                            rms_mode=1, page_size=PAGE, sm_scale=1 / 16))
+            slot_params.append(build_params(q, cache, o_s, l_s, bt, sl, **kw))
         o_m = torch.empty(nb, hs, RANK, dtype=torch.bfloat16, device=dev)
         lse_m = torch.empty(nb, hs, dtype=torch.float32, device=dev)
         params = slot_params[0]
     else:
         o = torch.empty(nb, H, RANK, dtype=torch.float32 if world > 1 else torch.bfloat16, device=dev)
         lse = torch.empty(nb, H, dtype=torch.float32, device=dev)
-        params = build_params(q, cache, o, lse, bt, sl, rank=RANK, qk_dim=QK, rms_offset=QK, rms_mode=1,
-                              page_size=PAGE, sm_scale=1 / 16)
+        params = build_params(q, cache, o, lse, bt, sl, **kw)
     run_params(params, dev)  # sizes and attaches the workspace once
     stream = torch.cuda.current_stream(dev)
     # our kernels per step: plan, decode, split merge (+ the P2P merge, or the NCCL path's correction)
@@ -334,7 +358,7 @@ def run_ours(args) -> None:
     value = total_bytes / (step_ms * 1e-3) / 1e12
     peak, peak_kind = measured_peak()
     achieved_gbs = mine / (decode_ms * 1e-3) / 1e9
-    traffic = profile_traffic() if world == 1 else None
+    traffic = profile_traffic() if world == 1 and not FP8 else None
     clocks = sampler.summary(t0, t1)
 
     # ---- end to end through the public entry point with host buffers (pinned) every step.
@@ -374,7 +398,7 @@ def run_ours(args) -> None:
         else:
             o_w, l_w = o, lse
         decode_attention_fwd(q_d, cache, cache[..., :RANK], o_w, l_w, bt_d, sl_d, logits, 8, 1 / 16, PAGE,
-                             is_mla=True, rms_offset=QK)
+                             is_mla=True, rms_offset=QK, k_scale=ks, v_scale=ks, rms_log8=FP8)
         if ex is not None:
             ex.merge(out=outs_dev[b][0], lse_out=outs_dev[b][1], mode="rs")
             res = outs_dev[b]
@@ -430,7 +454,7 @@ def run_ours(args) -> None:
     d2h = (outs_host[0][0].numel() * outs_host[0][0].element_size() + outs_host[0][1].numel() * 4) * world
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not FP8:
         cb, cs, n, threads = cpu_reference_sample(lens_all, args.cpu_budget)
         cpu = {"value": cb / cs / 1e12, "unit": "TB/s", "cores": threads, "kind": "port",
                "sample": f"{n} of the {nb} sequences ({cb / 1e9:.2f} GB of rows), numpy oracle, {cs:.1f} s"}
@@ -439,7 +463,7 @@ def run_ours(args) -> None:
         line = {
             "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp8-e4m3" if FP8 else "bf16",
             "data": "synthetic (seeded), random-init cache in the plugin's row layout",
             "config": {"workload": WORKLOAD if nb == B else f"{WORKLOAD} -- first {nb} sequences only",
                        "batch": nb, "heads": H, "rank": RANK, "rope": ROPE,
@@ -449,7 +473,7 @@ def run_ours(args) -> None:
                                         "scattered over ranks" if merge_kind == "p2p" else
                            "NCCL all-gather lse + correction kernel + reduce-scatter over heads"}
                           if world > 1 else {}),
-                       "l2": "inputs larger than L2 (2.44 GB cache), no flush"},
+                       "l2": f"inputs larger than L2 ({sum(lens_all) * ROW_READ / 1e9:.2f} GB of rows), no flush"},
             "seqs_per_s": nb / (step_ms * 1e-3),
             "hbm_frac_of_measured_peak": value * 1e3 / peak,
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
@@ -481,9 +505,15 @@ def main():
     ap.add_argument("--dcp-merge", choices=["p2p", "nccl"], default="p2p",
                     help="N>1: merge the ranks' partials with one kernel over NVLink peer memory "
                          "(default) or with NCCL (all-gather + correction + reduce-scatter)")
-    ap.add_argument("--batch", type=int, default=B,
+    ap.add_argument("--workload", choices=["cfg1", "cfg4"], default="cfg1",
+                    help="cfg1 (default, the headline): bf16 config 1; cfg4: FP8 8 x 262,144 tokens")
+    ap.add_argument("--batch", type=int, default=None,
                     help="first N sequences of config1 (smaller cases for ncu captures; default: all 64)")
     args = ap.parse_args()
+    if args.workload == "cfg4":
+        use_cfg4()
+    if args.batch is None:
+        args.batch = B
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

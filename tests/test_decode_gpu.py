@@ -79,11 +79,15 @@ def test_baseline_config0(cuda_device):
 
 
 @pytest.mark.parametrize("page", [1, 8, 16, 64, 400, 784])
-@pytest.mark.parametrize("path", ["tma", "cp_async"])
+@pytest.mark.parametrize("path", ["tma", "tma_one_column", "cp_async"])
 def test_pages_paths_ragged(cuda_device, page, path, monkeypatch):
-    """Every page size on both load paths, ragged lengths including 0, 1 and tile edges."""
+    """Every page size on every load path (TMA with the paired two-column K slots this shape
+    gets by default, TMA with one-column slots, cp.async), ragged lengths including 0, 1 and
+    tile edges."""
     if path == "cp_async":
         monkeypatch.setenv("QMLA_NO_TMA", "1")
+    if path == "tma_one_column":
+        monkeypatch.setenv("QMLA_NO_PAIR", "1")
     lens = [0, 1, 63, 64, 65, 1000, 2049, 130]
     cache, q, bt, sl = make_bf16_case(len(lens), 24, 768, 232, page, lens, seed=page, device=cuda_device)
     o, lse = _run(q, cache, bt, sl, rank=768, rms_offset=1000, page=page)
@@ -109,9 +113,11 @@ def test_fp8_modes(cuda_device, mode, page):
 
 
 @pytest.mark.parametrize("heads,rank,rope", [(12, 384, 116), (16, 512, 128), (32, 256, 232), (8, 768, 232),
-                                             (32, 768, 232)])
+                                             (32, 768, 232), (24, 768, 256), (24, 768, 64)])
 def test_head_and_rank_shapes(cuda_device, heads, rank, rope):
-    """GLA-g2 groups (12 heads, 384 | 116) and the other head counts / ranks the kernel is built for."""
+    """GLA-g2 groups (12 heads, 384 | 116) and the other head counts / ranks the kernel is built for.
+    Rank 768 with rope 256 (no partial last column) and rope 64 (an odd number of full columns:
+    the last paired slot holds one column) cover the paired layout's edges."""
     lens = [300, 4097, 5]
     cache, q, bt, sl = make_bf16_case(len(lens), heads, rank, rope, 16, lens, seed=heads, device=cuda_device)
     qk = rank + rope
