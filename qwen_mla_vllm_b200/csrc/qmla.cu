@@ -454,6 +454,9 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
   a.n_qk_slots = pl.n_qk_slots;
   a.n_sub_qk = pl.n_sub_qk;
   a.n_full_chunks = pl.n_full_chunks;
+  // a row segment's fixed overhead, in tiles, for the work partition (test hook QMLA_SEG_COST)
+  a.seg_cost = 2;  // swept 0-4: 2 best on a DCP rank's shard (+17% over 0), config 1 and GLA flat
+  if (const char* e = getenv("QMLA_SEG_COST")) a.seg_cost = std::max(0, std::min(atoi(e), 64));
 
   a.rms_base_b = pl.rms_base_b;
   a.rms_units = pl.rms_units;

@@ -76,17 +76,42 @@ __global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
                        -INFINITY);
     return;
   }
-  const int tpc = (total + a.G - 1) / a.G;
-  const int c0 = plo / tpc, c1 = (phi - 1) / tpc;
+  (void)total;
+  // CTA ranges that hold tiles of this row (range_bound: the decode kernel's partition)
+  auto cta_of = [&](int t) {  // the non-empty range holding tile t: largest c with bound(c) <= t
+    int lo = 0, hi = a.G;
+    while (hi - lo > 1) {
+      const int m = (lo + hi) >> 1;
+      if (range_bound(a.tile_prefix, a.num_rows, a.G, a.seg_cost, m) <= t)
+        lo = m;
+      else
+        hi = m;
+    }
+    return lo;
+  };
+  __shared__ int c0_s, c1_s;
+  if (threadIdx.x == 0) {
+    c0_s = cta_of(plo);
+    c1_s = cta_of(phi - 1);
+  }
+  __syncthreads();
+  const int c0 = c0_s, c1 = c1_s;
   if (c0 == c1) return;  // the row lies inside one CTA range: already final
   __shared__ float wts[kMaxCtas];
   __shared__ int slots[kMaxCtas];
   __shared__ float lse_g;
-  const int np = c1 - c0 + 1;  // <= G <= kMaxCtas
-  for (int i = threadIdx.x; i < np; i += blockDim.x) {
-    const int c = c0 + i;
-    slots[i] = (plo <= c * tpc) ? 2 * c : 2 * c + 1;
+  __shared__ int np_s;
+  if (threadIdx.x == 0) {
+    int np = 0;  // empty ranges between c0 and c1 wrote nothing
+    for (int c = c0; c <= c1; ++c) {
+      const int lo_c = range_bound(a.tile_prefix, a.num_rows, a.G, a.seg_cost, c);
+      const int hi_c = range_bound(a.tile_prefix, a.num_rows, a.G, a.seg_cost, c + 1);
+      if (lo_c < hi_c) slots[np++] = (plo <= lo_c) ? 2 * c : 2 * c + 1;
+    }
+    np_s = np;
   }
+  __syncthreads();
+  const int np = np_s;
   __syncthreads();
   if (threadIdx.x == 0) {
     float m = -INFINITY;

@@ -99,6 +99,7 @@ struct DecodeArgs {
   int n_qk_slots;   // K-ring slots loaded per tile (two 128-byte column chunks per slot)
   int n_sub_qk;     // 128-byte-wide MMA sub-chunks of the QK width
   int n_full_chunks;  // chunks that lie entirely inside the QK width
+  int seg_cost;       // work-partition cost of a row's segment overhead, in tiles
   int rms_base_b;   // 16-byte-aligned first byte of the rms tail in a row
   int rms_units;    // 16-byte units staged per token (0: no rms); staging stride = 16 * rms_units
   int rms_skip;     // first rms byte within the staged units
@@ -197,6 +198,33 @@ __device__ __forceinline__ bool next_segment(const int32_t* prefix, SegCursor& c
   c.lo = end;
   ++c.row;
   return true;
+}
+
+// First tile of CTA range c (c = 0..G; range c is [bound(c), bound(c+1))).  The tiles are
+// split so that every CTA gets an equal share of the cost tiles + seg_cost * rows: a row's
+// segment overhead (Q staging, pipeline refill, epilogue) counts as seg_cost tiles at its
+// start.  A boundary that falls inside that overhead maps to the row's first tile, so a
+// range can be empty.  Depends only on the lengths: the partition, and with it every
+// reduction order, is the same for the same inputs.
+__device__ __forceinline__ int range_bound(const int32_t* prefix, int n, int G, int seg_cost, int c) {
+  const int T = __ldg(prefix + n);
+  if (c <= 0) return 0;
+  if (c >= G) return T;
+  const int64_t C = (int64_t)T + (int64_t)seg_cost * n;
+  const int64_t x = C * c / G;
+  int lo = 0, hi = n;  // cost(lo) <= x < cost(hi), cost(r) = prefix[r] + seg_cost * r
+  while (hi - lo > 1) {
+    const int m = (lo + hi) >> 1;
+    if ((int64_t)__ldg(prefix + m) + (int64_t)seg_cost * m <= x)
+      lo = m;
+    else
+      hi = m;
+  }
+  const int p0 = __ldg(prefix + lo), p1 = __ldg(prefix + lo + 1);
+  int64_t off = x - ((int64_t)p0 + (int64_t)seg_cost * lo) - seg_cost;
+  off = off < 0 ? 0 : off;
+  off = off > (int64_t)(p1 - p0) ? (int64_t)(p1 - p0) : off;
+  return p0 + (int)off;
 }
 
 // Row of the segment next_segment() would return next, or -1 (the cursor is not moved).
@@ -334,9 +362,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 
   // ------------------------------------------------ work range
   const int total = __ldg(a.tile_prefix + a.num_rows);
-  const int tpc = (total + a.G - 1) / a.G;
-  const int range_lo = blockIdx.x * tpc;
-  const int range_hi = min(total, range_lo + tpc);
+  const int range_lo = range_bound(a.tile_prefix, a.num_rows, a.G, a.seg_cost, (int)blockIdx.x);
+  const int range_hi = range_bound(a.tile_prefix, a.num_rows, a.G, a.seg_cost, (int)blockIdx.x + 1);
+  (void)total;
   if (range_lo >= range_hi) return;  // uniform for the whole CTA
   const int row0 = first_row_at(a.tile_prefix, a.num_rows, range_lo);
 #ifdef QMLA_TRACE
