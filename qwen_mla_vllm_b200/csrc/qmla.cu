@@ -139,7 +139,7 @@ struct Plan {
   int G;
   int q_vec, qpe_vec;
   // workspace offsets
-  int64_t ws_status, ws_prefix, ws_plse, ws_po, ws_total;
+  int64_t ws_status, ws_bounds, ws_prefix, ws_plse, ws_po, ws_total;
   // smem
   uint32_t off_kring, nk, off_vring, nv, off_q, q_chunk, off_p, p_bytes, off_rms, off_misc;
   uint32_t smem_total;
@@ -281,6 +281,8 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   int64_t w = 0;
   pl->ws_status = w;
   w += 256;
+  pl->ws_bounds = w;
+  w = align_up(w + 4 * ((int64_t)kMaxCtas + 1), 256);
   pl->ws_prefix = w;
   w = align_up(w + 4 * ((int64_t)p->num_rows + 1), 256);
   pl->ws_plse = w;
@@ -476,6 +478,7 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
   a.tile_prefix = p->plan_tile_prefix ? p->plan_tile_prefix
                                       : reinterpret_cast<const int32_t*>(ws + pl.ws_prefix);
   a.part_lse = reinterpret_cast<float*>(ws + pl.ws_plse);
+  a.range_bounds = reinterpret_cast<const int32_t*>(ws + pl.ws_bounds);
   a.part_o = reinterpret_cast<float*>(ws + pl.ws_po);
   a.G = pl.G;
   a.off_kring = pl.off_kring;
@@ -502,11 +505,14 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
     rc = cache_tensor_map(p, pl.run, &maps);
     if (rc != QMLA_OK) return rc;
   }
+  int32_t* bounds = reinterpret_cast<int32_t*>(ws + pl.ws_bounds);
   if (!p->plan_tile_prefix) {
     plan_kernel<<<1, 1024, 0, st>>>(p->seq_lens, p->num_rows,
-                                    reinterpret_cast<int32_t*>(ws + pl.ws_prefix), a.status);
+                                    reinterpret_cast<int32_t*>(ws + pl.ws_prefix), a.status,
+                                    a.G, a.seg_cost, bounds);
   } else {
-    if (cudaMemsetAsync(a.status, 0, 4, st) != cudaSuccess) return QMLA_E_CUDA;
+    bounds_kernel<<<1, 256, 0, st>>>(p->plan_tile_prefix, p->num_rows, a.status, a.G, a.seg_cost,
+                                     bounds);
   }
   if (cudaGetLastError() != cudaSuccess) return QMLA_E_CUDA;
   rc = launch_decode(p->kv_dtype == QMLA_DT_FP8E4M3, pl.cps == 2, pl.nb, pl.nqk, maps, a,

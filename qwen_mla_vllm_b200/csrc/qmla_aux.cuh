@@ -10,12 +10,14 @@
 
 namespace qmla {
 
-// Exclusive prefix of ceil(max(len,0)/kTile) over the rows, plus the total, and
-// clears the device status word.  One block of 1024 threads.
-// Partition rule shared with the host planner (qmla_plan).
+// Exclusive prefix of ceil(max(len,0)/kTile) over the rows, plus the total, the G + 1
+// CTA range bounds of the decode kernel's partition (range_bound), and clears the device
+// status word.  One block of 1024 threads.  Partition rule shared with the host planner
+// (qmla_plan) for the prefix.
 __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ seq_lens, int n,
                                                     int32_t* __restrict__ prefix,
-                                                    int* __restrict__ status) {
+                                                    int* __restrict__ status, int G, int seg_cost,
+                                                    int32_t* __restrict__ bounds) {
   __shared__ int warp_sums[32];
   __shared__ int carry_s;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -56,6 +58,19 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
     if (tid == 1023) carry_s = incl;
     __syncthreads();
   }
+  __threadfence_block();
+  __syncthreads();  // the prefix is complete (global writes of this block are visible to it)
+  for (int c = tid; c <= G; c += blockDim.x) bounds[c] = range_bound(prefix, n, G, seg_cost, c);
+}
+
+// The range bounds alone, for a prefix planned on the host (qmla_plan); also clears the
+// device status word.  One block.
+__global__ void __launch_bounds__(256) bounds_kernel(const int32_t* __restrict__ prefix, int n,
+                                                     int* __restrict__ status, int G, int seg_cost,
+                                                     int32_t* __restrict__ bounds) {
+  if (threadIdx.x == 0 && status) *status = 0;
+  for (int c = threadIdx.x; c <= G; c += blockDim.x)
+    bounds[c] = range_bound(prefix, n, G, seg_cost, c);
 }
 
 // Merge of the per-CTA partial segments of rows that crossed a CTA boundary
@@ -77,25 +92,22 @@ __global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
     return;
   }
   (void)total;
-  // CTA ranges that hold tiles of this row (range_bound: the decode kernel's partition)
-  auto cta_of = [&](int t) {  // the non-empty range holding tile t: largest c with bound(c) <= t
+  // CTA ranges that hold tiles of this row (the decode kernel's partition, range_bounds)
+  __shared__ int bnd[kMaxCtas + 1];
+  for (int c = threadIdx.x; c <= a.G; c += blockDim.x) bnd[c] = __ldg(a.range_bounds + c);
+  __syncthreads();
+  auto cta_of = [&](int t) {  // the non-empty range holding tile t: largest c with bnd[c] <= t
     int lo = 0, hi = a.G;
     while (hi - lo > 1) {
       const int m = (lo + hi) >> 1;
-      if (range_bound(a.tile_prefix, a.num_rows, a.G, a.seg_cost, m) <= t)
+      if (bnd[m] <= t)
         lo = m;
       else
         hi = m;
     }
     return lo;
   };
-  __shared__ int c0_s, c1_s;
-  if (threadIdx.x == 0) {
-    c0_s = cta_of(plo);
-    c1_s = cta_of(phi - 1);
-  }
-  __syncthreads();
-  const int c0 = c0_s, c1 = c1_s;
+  const int c0 = cta_of(plo), c1 = cta_of(phi - 1);
   if (c0 == c1) return;  // the row lies inside one CTA range: already final
   __shared__ float wts[kMaxCtas];
   __shared__ int slots[kMaxCtas];
@@ -103,11 +115,8 @@ __global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
   __shared__ int np_s;
   if (threadIdx.x == 0) {
     int np = 0;  // empty ranges between c0 and c1 wrote nothing
-    for (int c = c0; c <= c1; ++c) {
-      const int lo_c = range_bound(a.tile_prefix, a.num_rows, a.G, a.seg_cost, c);
-      const int hi_c = range_bound(a.tile_prefix, a.num_rows, a.G, a.seg_cost, c + 1);
-      if (lo_c < hi_c) slots[np++] = (plo <= lo_c) ? 2 * c : 2 * c + 1;
-    }
+    for (int c = c0; c <= c1; ++c)
+      if (bnd[c] < bnd[c + 1]) slots[np++] = (plo <= bnd[c]) ? 2 * c : 2 * c + 1;
     np_s = np;
   }
   __syncthreads();

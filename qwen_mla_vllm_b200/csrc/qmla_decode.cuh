@@ -116,7 +116,8 @@ struct DecodeArgs {
   int lse_dtype;
   // workspace
   int* status;
-  const int32_t* tile_prefix;  // [num_rows + 1]
+  const int32_t* tile_prefix;   // [num_rows + 1]
+  const int32_t* range_bounds;  // [G + 1] first tile of each CTA range (range_bound)
   float* part_o;               // [2*G][H][rank]
   float* part_lse;             // [2*G][H] (log2 units)
   int G;
@@ -206,8 +207,9 @@ __device__ __forceinline__ bool next_segment(const int32_t* prefix, SegCursor& c
 // start.  A boundary that falls inside that overhead maps to the row's first tile, so a
 // range can be empty.  Depends only on the lengths: the partition, and with it every
 // reduction order, is the same for the same inputs.
+// Plain loads: the plan kernel calls it on the prefix it has just written.
 __device__ __forceinline__ int range_bound(const int32_t* prefix, int n, int G, int seg_cost, int c) {
-  const int T = __ldg(prefix + n);
+  const int T = prefix[n];
   if (c <= 0) return 0;
   if (c >= G) return T;
   const int64_t C = (int64_t)T + (int64_t)seg_cost * n;
@@ -215,12 +217,12 @@ __device__ __forceinline__ int range_bound(const int32_t* prefix, int n, int G, 
   int lo = 0, hi = n;  // cost(lo) <= x < cost(hi), cost(r) = prefix[r] + seg_cost * r
   while (hi - lo > 1) {
     const int m = (lo + hi) >> 1;
-    if ((int64_t)__ldg(prefix + m) + (int64_t)seg_cost * m <= x)
+    if ((int64_t)prefix[m] + (int64_t)seg_cost * m <= x)
       lo = m;
     else
       hi = m;
   }
-  const int p0 = __ldg(prefix + lo), p1 = __ldg(prefix + lo + 1);
+  const int p0 = prefix[lo], p1 = prefix[lo + 1];
   int64_t off = x - ((int64_t)p0 + (int64_t)seg_cost * lo) - seg_cost;
   off = off < 0 ? 0 : off;
   off = off > (int64_t)(p1 - p0) ? (int64_t)(p1 - p0) : off;
@@ -362,8 +364,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 
   // ------------------------------------------------ work range
   const int total = __ldg(a.tile_prefix + a.num_rows);
-  const int range_lo = range_bound(a.tile_prefix, a.num_rows, a.G, a.seg_cost, (int)blockIdx.x);
-  const int range_hi = range_bound(a.tile_prefix, a.num_rows, a.G, a.seg_cost, (int)blockIdx.x + 1);
+  const int range_lo = __ldg(a.range_bounds + blockIdx.x);
+  const int range_hi = __ldg(a.range_bounds + blockIdx.x + 1);
   (void)total;
   if (range_lo >= range_hi) return;  // uniform for the whole CTA
   const int row0 = first_row_at(a.tile_prefix, a.num_rows, range_lo);
