@@ -234,6 +234,137 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------ context gather
+# --workload gather: the chunked-prefill context gather (qmla_gather_cache) on one GPU.  Not the
+# headline line.  A 131,072-row chunk (16 sequences x 8192 tokens) of an FP8 cache (row 768|232
+# e4m3 + 24 log8 codes = 1024 B), pages in random order, into a bf16 [rows, 1024] destination.
+GATHER_SEQS, GATHER_LEN = 16, 8192
+GATHER_WORKLOAD = ("prefill context gather: FP8-e4m3 cache rows (768|232 e4m3 + 24 log8 codes, 1024 B) "
+                   "-> bf16 [131072, 1024], 16 sequences x 8192 tokens, 16-token pages in random order")
+GATHER_METRIC = "MLA prefill context gather achieved HBM GB/s (FP8 -> bf16 dequant)"
+
+
+def gather_row_bytes() -> float:
+    """Algorithmic bytes per destination row: the cache row read, the bf16 row written, the
+    token's sequence id, and its share of one block-table entry per page."""
+    return ROW + 2 * (QK + H) + 4 + 4 / PAGE
+
+
+def run_gather(args) -> None:
+    import torch
+    if int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        raise SystemExit("--workload gather runs on one GPU")
+    from qwen_mla_vllm_b200.mla_gather import gather_cache_torch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    seqs, L = GATHER_SEQS, GATHER_LEN
+    n = seqs * L
+    P = n // PAGE
+    gd = torch.Generator(device=dev).manual_seed(7)
+    raw = torch.randint(0, 256, (P, PAGE, 1, ROW), dtype=torch.uint8, device=dev, generator=gd)
+    raw[..., :QK] = (torch.randn(P, PAGE, 1, QK, device=dev, generator=gd) * 100).clamp(-448, 448) \
+        .to(torch.float8_e4m3fn).view(torch.uint8)
+    cache = raw.view(torch.float8_e4m3fn)
+    g = torch.Generator().manual_seed(7)
+    bt_h = torch.randperm(P, generator=g).reshape(seqs, L // PAGE).to(torch.int32)
+    cu_h = torch.arange(0, (seqs + 1) * L, L, dtype=torch.int32)
+    t2s_h = torch.arange(seqs, dtype=torch.int32).repeat_interleave(L)
+    bt, cu, t2s = bt_h.to(dev), cu_h.to(dev), t2s_h.to(dev)
+    scale = torch.tensor(0.01, device=dev)
+    dst = torch.empty(n, ROW, dtype=torch.bfloat16, device=dev)
+    kw = dict(src_cache=cache, kv_cache_dtype="fp8", scale=scale, mla_rms=(QK, H, "log8"))
+
+    def step(out, b, c, t):
+        gather_cache_torch(dst=out, block_table=b, cu_seq_lens=c, token_to_seq=t, num_tokens=n, **kw)
+
+    step(dst, bt, cu, t2s)
+    torch.cuda.synchronize()
+    t_end = time.perf_counter() + 1.0  # clock ramp
+    while time.perf_counter() < t_end:
+        for _ in range(20):
+            step(dst, bt, cu, t2s)
+        torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        step(dst, bt, cu, t2s)
+    stream = torch.cuda.current_stream(dev)
+    sampler = ClockSampler(0).start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        step(dst, bt, cu, t2s)
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    sampler.stop()
+    per = [a.elapsed_time(b) for a, b in ev]
+    step_ms = statistics.mean(per)
+    total = n * gather_row_bytes()
+    gbs = total / (step_ms * 1e-3) / 1e9
+    peak, peak_kind = measured_peak()
+
+    # end to end: the step's index tables from pinned host memory in, the destination out
+    bt_p, cu_p, t2s_p = bt_h.pin_memory(), cu_h.pin_memory(), t2s_h.pin_memory()
+    dst_h = torch.empty(n, ROW, dtype=torch.bfloat16).pin_memory()
+    bt_d, cu_d, t2s_d = torch.empty_like(bt), torch.empty_like(cu), torch.empty_like(t2s)
+
+    def e2e_step():
+        bt_d.copy_(bt_p, non_blocking=True)
+        cu_d.copy_(cu_p, non_blocking=True)
+        t2s_d.copy_(t2s_p, non_blocking=True)
+        step(dst, bt_d, cu_d, t2s_d)
+        dst_h.copy_(dst, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    h2d = bt_h.numel() * 4 + cu_h.numel() * 4 + t2s_h.numel() * 4
+    d2h = dst_h.numel() * 2
+
+    cpu = None
+    if not args.no_cpu_baseline:  # the oracle's gather on a bounded sample of the same chunk
+        import oracle
+        sample = min(n, 16384)
+        rows_np = raw[:, :, 0, :].cpu().numpy()
+        bt_np, cu_np, t2s_np = bt_h.numpy(), cu_h.numpy(), t2s_h.numpy()
+        reps, spent = 0, 0.0
+        while spent < args.cpu_budget:
+            c0 = time.perf_counter()
+            vals = oracle.gather_cache(rows_np, bt_np, cu_np, t2s_np, sample, fp8=True, scale=0.01,
+                                       mla_rms=(QK, H, "log8"))
+            oracle.f32_to_bf16_bits(vals)
+            spent += time.perf_counter() - c0
+            reps += 1
+        cpu = {"value": reps * sample * gather_row_bytes() / spent / 1e9, "unit": "GB/s", "cores": 1,
+               "kind": "port", "sample": f"{reps} x the first {sample} rows of the chunk, numpy oracle "
+                                         f"(gather + bf16 rounding), {spent:.1f} s"}
+    clocks = sampler.summary(t0, t1)
+    line = {
+        "metric": GATHER_METRIC, "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp8-e4m3->bf16", "data": "synthetic (seeded)",
+        "config": {"workload": GATHER_WORKLOAD, "rows": n, "row_bytes_read": ROW, "dst_bytes_per_row": 2 * ROW,
+                   "l2": f"inputs larger than L2 ({n * gather_row_bytes() / 1e6:.0f} MB moved per step), no flush"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                     "traffic": None, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                     "kernel": "gather_cache_kernel (one launch per step)"},
+        "cpu_baseline": cpu,
+        "e2e": {"value": total / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+        "gpu_launches": args.steps,
+    }
+    print(json.dumps(line), flush=True)
+
+
 # ------------------------------------------------------------------------------ GPU arm
 def run_ours(args) -> None:
     import torch
@@ -505,8 +636,9 @@ def main():
     ap.add_argument("--dcp-merge", choices=["p2p", "nccl"], default="p2p",
                     help="N>1: merge the ranks' partials with one kernel over NVLink peer memory "
                          "(default) or with NCCL (all-gather + correction + reduce-scatter)")
-    ap.add_argument("--workload", choices=["cfg1", "cfg4"], default="cfg1",
-                    help="cfg1 (default, the headline): bf16 config 1; cfg4: FP8 8 x 262,144 tokens")
+    ap.add_argument("--workload", choices=["cfg1", "cfg4", "gather"], default="cfg1",
+                    help="cfg1 (default, the headline): bf16 config 1; cfg4: FP8 8 x 262,144 tokens; "
+                         "gather: the prefill context gather on one GPU")
     ap.add_argument("--batch", type=int, default=None,
                     help="first N sequences of config1 (smaller cases for ncu captures; default: all 64)")
     args = ap.parse_args()
@@ -516,7 +648,11 @@ def main():
         args.batch = B
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.workload == "gather":
+        if args.impl == "reference":
+            raise SystemExit("--workload gather has no reference arm; its line carries cpu_baseline")
+        run_gather(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -28,6 +28,8 @@
  *                        fused into one merge of N (out, lse) partials.
  *   qmla_fp8_cache_write <- qwen_mla/mla_impl.py:309-342
  *                        (QwenMLATritonImpl.do_kv_cache_update, FP8 row writer).
+ *   qmla_gather_cache <- qwen_mla/ops/mla_gather.py:28-76 (gather_cache_torch, the
+ *                        chunked-prefill context gather with FP8 dequantisation).
  *   qmla_dcp_p2p_merge <- the same cp_lse_ag_out_rs sequence (dcp_fix.py:133-142)
  *                        done by one kernel over NVLink peer memory instead of
  *                        NCCL; no counterpart in the reference, which refuses
@@ -189,6 +191,44 @@ int qmla_fp8_cache_write(const void* latent, int64_t latent_stride, const void* 
                          int32_t rank, int32_t rope, int32_t heads, int32_t rms_mode,
                          const float* k_scale, void* cache, int64_t cache_row_stride,
                          void* stream);
+
+/* ---- prefill context gather ----------------------------------------------
+ * (qwen_mla/ops/mla_gather.py:28-76)  Destination row j (0 <= j < num_tokens)
+ * belongs to sequence s = token_to_seq[j] and holds that sequence's token
+ *   tok = j - cu_seq_lens[s] + (seq_starts ? seq_starts[s] : 0),
+ * read from page block_table[s * block_table_stride + tok / page_size] at offset
+ * tok % page_size.
+ *   2-byte cache (QMLA_DT_BF16 / F16): the first row_elems elements of the row are
+ *     copied, converted to dst_dtype.
+ *   FP8 cache: columns [0, rms_offset) become e4m3 * (*scale); the rms_heads columns
+ *     from rms_offset are decoded per rms_mode: QMLA_RMS_LOG8 (one code byte per
+ *     head, 2^(-3 + code * 6/255)), QMLA_RMS_BF16 (two raw bf16 bytes per head) or
+ *     QMLA_RMS_NATIVE (e4m3 * scale, like the latent).  Later columns are untouched.
+ * Rows whose sequence, token or page index falls outside the tables are skipped and
+ * set bit 2 of *status (when status is not NULL). */
+typedef struct qmla_gather_params {
+  const void* src_cache;                    /* element (p, t, c) at p*stride_page + t*stride_token + c */
+  int64_t src_stride_page, src_stride_token; /* elements of src_dtype */
+  int32_t page_size, num_pages;
+  int32_t src_dtype;                        /* QMLA_DT_BF16, QMLA_DT_F16 or QMLA_DT_FP8E4M3 */
+  int32_t row_elems;                        /* 2-byte cache: elements copied per row */
+  int32_t rms_offset, rms_heads, rms_mode;  /* FP8 cache only */
+  const float* scale;                       /* FP8 cache: per-layer scale (device scalar) */
+  const int32_t* block_table;               /* [num_seqs][block_table_cols] page ids */
+  int64_t block_table_stride;
+  int32_t block_table_cols;
+  const int32_t* cu_seq_lens;               /* [num_seqs + 1] first destination row of each sequence */
+  const int32_t* token_to_seq;              /* [num_tokens] */
+  const int32_t* seq_starts;                /* [num_seqs] first token of the chunk, or NULL */
+  int32_t num_seqs, num_tokens;
+  void* dst;                                /* [num_tokens][dst_stride_row] */
+  int64_t dst_stride_row;                   /* elements of dst_dtype */
+  int32_t dst_dtype;                        /* QMLA_DT_BF16, QMLA_DT_F16 or QMLA_DT_F32 */
+  int32_t* status;                          /* optional device word; bit 2 = bad index */
+  int32_t device;
+} qmla_gather_params;
+
+int qmla_gather_cache(const qmla_gather_params* p, void* stream);
 
 /* ---- DCP over NVLink peer memory ------------------------------------------
  * Each rank of a DCP group (one process per GPU) owns one exchange buffer:

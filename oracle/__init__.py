@@ -13,11 +13,11 @@ reference's own torch functions (``tests/golden/make_golden.py``); see
 """
 from .numerics import (bf16_bits_to_f32, bf16_round, e4m3_decode, e4m3_encode, f32_to_bf16_bits,
                        log8_decode, log8_encode)
-from .decode import (TILE, dcp_correct, dcp_merge, decode, fp8_cache_rows, mtp_flatten,
-                     plan_arrays, rank_plan_arrays, tile_prefix)
+from .decode import (TILE, dcp_correct, dcp_merge, decode, fp8_cache_rows, gather_cache,
+                     mtp_flatten, plan_arrays, rank_plan_arrays, tile_prefix)
 
 __all__ = [
     "TILE", "bf16_bits_to_f32", "bf16_round", "e4m3_decode", "e4m3_encode", "f32_to_bf16_bits",
-    "log8_decode", "log8_encode", "dcp_correct", "dcp_merge", "decode", "fp8_cache_rows",
+    "log8_decode", "log8_encode", "dcp_correct", "dcp_merge", "decode", "fp8_cache_rows", "gather_cache",
     "mtp_flatten", "plan_arrays", "rank_plan_arrays", "tile_prefix",
 ]

@@ -156,6 +156,52 @@ def fp8_cache_rows(latent: np.ndarray, k_pe: np.ndarray, k_scale: float, packed_
     return np.concatenate([lat, rope, rms], axis=1)
 
 
+def gather_cache(cache: np.ndarray, block_table: np.ndarray, cu_seq_lens: np.ndarray,
+                 token_to_seq: np.ndarray, num_tokens: int, *, fp8: bool, scale: float = 1.0,
+                 seq_starts: np.ndarray | None = None, mla_rms: tuple | None = None) -> np.ndarray:
+    """Chunked-prefill context gather: the float32 values of the destination columns it writes.
+
+    qwen_mla/ops/mla_gather.py:28-76 (gather_cache_torch).  Row j of the destination is
+    token tok = j - cu_seq_lens[s] (+ seq_starts[s]) of sequence s = token_to_seq[j], read
+    from page block_table[s, tok // page] at tok % page.  ``cache`` is [pages, page, width]:
+    uint16 bf16 bit patterns (2-byte cache, the whole row is copied) or uint8 bytes (FP8).
+    Index arithmetic :41-47; the 2-byte copy :48-50.  FP8 rows: columns [0, off) =
+    e4m3 * scale in float32 (:69); the heads columns from off are the log8 code decoded
+    (:70-74), the raw bf16 bytes (:75-76) or, in "e4m3" mode, e4m3 * scale like the
+    latent (:66-68).  ``mla_rms`` = (off, heads[, mode]) with mode "bf16" by default
+    (:58-59).  The reference's slicing into 8192-row passes (:61-65) does not change the
+    values.  The caller rounds to the destination dtype.
+    """
+    n = int(num_tokens)
+    if n <= 0:
+        return np.zeros((0, 0), np.float32)
+    page = cache.shape[1]
+    j = np.arange(n, dtype=np.int64)
+    s = np.asarray(token_to_seq, dtype=np.int64)[:n]
+    tok = j - np.asarray(cu_seq_lens, dtype=np.int64)[s]
+    if seq_starts is not None:
+        tok = tok + np.asarray(seq_starts, dtype=np.int64)[s]
+    blk = np.asarray(block_table, dtype=np.int64)[s, tok // page]
+    rows = cache[blk, tok % page].reshape(n, -1)
+    if not fp8:
+        return bf16_bits_to_f32(rows)
+    if mla_rms is None:
+        raise NotImplementedError("FP8 MLA gather needs the row layout (rms offset, heads)")
+    off, nh = int(mla_rms[0]), int(mla_rms[1])
+    mode = mla_rms[2] if len(mla_rms) > 2 else "bf16"
+    sc = np.float32(scale)
+    if mode == "e4m3":
+        return (e4m3_decode(rows[:, :off + nh]) * sc).astype(np.float32)
+    out = np.empty((n, off + nh), np.float32)
+    out[:, :off] = e4m3_decode(rows[:, :off]) * sc
+    if mode == "log8":
+        out[:, off:] = log8_decode(rows[:, off:off + nh])
+    else:
+        b = rows[:, off:off + 2 * nh].astype(np.uint16)
+        out[:, off:] = bf16_bits_to_f32(b[:, 0::2] | (b[:, 1::2] << 8))
+    return out
+
+
 def dcp_correct(out: np.ndarray, lses: np.ndarray, cp_rank: int, is_base_e: bool = True):
     """One rank's DCP output correction: returns (out * exp(lse_rank - lse_global), lse_global).
 

@@ -109,6 +109,40 @@ class DcpP2PParams(ctypes.Structure):
     ]
 
 
+class GatherParams(ctypes.Structure):
+    """Mirror of ``qmla_gather_params`` (field order and types must match qmla.h)."""
+
+    _fields_ = [
+        ("src_cache", ctypes.c_void_p),
+        ("src_stride_page", ctypes.c_int64),
+        ("src_stride_token", ctypes.c_int64),
+        ("page_size", ctypes.c_int32),
+        ("num_pages", ctypes.c_int32),
+        ("src_dtype", ctypes.c_int32),
+        ("row_elems", ctypes.c_int32),
+        ("rms_offset", ctypes.c_int32),
+        ("rms_heads", ctypes.c_int32),
+        ("rms_mode", ctypes.c_int32),
+        ("scale", ctypes.c_void_p),
+        ("block_table", ctypes.c_void_p),
+        ("block_table_stride", ctypes.c_int64),
+        ("block_table_cols", ctypes.c_int32),
+        ("cu_seq_lens", ctypes.c_void_p),
+        ("token_to_seq", ctypes.c_void_p),
+        ("seq_starts", ctypes.c_void_p),
+        ("num_seqs", ctypes.c_int32),
+        ("num_tokens", ctypes.c_int32),
+        ("dst", ctypes.c_void_p),
+        ("dst_stride_row", ctypes.c_int64),
+        ("dst_dtype", ctypes.c_int32),
+        ("status", ctypes.c_void_p),
+        ("device", ctypes.c_int32),
+    ]
+
+
+# device status bits (qmla_read_status / the gather's status word)
+DEV_ERR_TIMEOUT, DEV_ERR_INDEX = 1, 2
+
 # exported symbols and their ctypes prototypes: (restype, argtypes)
 _VP, _I32, _I64, _F32P = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p
 PROTOTYPES = {
@@ -131,6 +165,7 @@ PROTOTYPES = {
     "qmla_dcp_buffer_free": (ctypes.c_int, [_VP]),
     "qmla_dcp_p2p_merge": (ctypes.c_int, [ctypes.POINTER(DcpP2PParams), _VP]),
     "qmla_dcp_read_status": (ctypes.c_int, [_VP, _VP, ctypes.POINTER(_I32)]),
+    "qmla_gather_cache": (ctypes.c_int, [ctypes.POINTER(GatherParams), _VP]),
 }
 
 _lib = None

@@ -4,12 +4,13 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <map>
-#include <tuple>
 #include <mutex>
+#include <tuple>
 
 #include "qmla.h"
 #include "qmla_aux.cuh"
@@ -378,7 +379,7 @@ extern "C" {
 void qmla_set_trace(void* dev_ptr) { g_trace = reinterpret_cast<unsigned long long*>(dev_ptr); }
 #endif
 
-int qmla_abi_version(void) { return 101; }
+int qmla_abi_version(void) { return 102; }
 
 const char* qmla_error_string(int code) {
   switch (code) {
@@ -723,6 +724,87 @@ int qmla_fp8_cache_write(const void* latent, int64_t latent_stride, const void* 
       reinterpret_cast<const __nv_bfloat16*>(latent), latent_stride,
       reinterpret_cast<const __nv_bfloat16*>(k_pe), k_pe_stride, slot_mapping, rank, rope, heads,
       rms_mode, k_scale, reinterpret_cast<uint8_t*>(cache), cache_row_stride);
+  return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
+}
+
+int qmla_gather_cache(const qmla_gather_params* p, void* stream) {
+  if (!p || p->num_tokens < 0 || p->num_seqs < 0) return QMLA_E_INVALID;
+  if (p->num_tokens == 0) return QMLA_OK;
+  if (!p->src_cache || !p->dst || !p->block_table || !p->cu_seq_lens || !p->token_to_seq ||
+      p->page_size <= 0 || p->num_pages <= 0 || p->block_table_cols <= 0 ||
+      p->src_stride_page < 0 || p->src_stride_token < 0 || p->dst_stride_row < 0)
+    return QMLA_E_INVALID;
+  if (p->dst_dtype != QMLA_DT_BF16 && p->dst_dtype != QMLA_DT_F16 && p->dst_dtype != QMLA_DT_F32)
+    return QMLA_E_UNSUPPORTED;
+  const bool fp8 = p->src_dtype == QMLA_DT_FP8E4M3;
+  if (!fp8 && p->src_dtype != QMLA_DT_BF16 && p->src_dtype != QMLA_DT_F16) return QMLA_E_UNSUPPORTED;
+  GatherArgs a;
+  memset(&a, 0, sizeof(a));
+  const int se = fp8 ? 1 : 2, de = p->dst_dtype == QMLA_DT_F32 ? 4 : 2;
+  int64_t src_row = 0, dst_cols = 0;
+  if (fp8) {
+    if (p->rms_offset <= 0 || p->rms_heads < 0 || !p->scale) return QMLA_E_INVALID;
+    if (p->rms_mode == QMLA_RMS_NATIVE) {
+      a.n_e4m3 = p->rms_offset + p->rms_heads;
+      src_row = a.n_e4m3;
+    } else if (p->rms_mode == QMLA_RMS_LOG8 || p->rms_mode == QMLA_RMS_BF16) {
+      a.n_e4m3 = p->rms_offset;
+      a.rms_heads = p->rms_heads;
+      a.rms_off = p->rms_offset;
+      a.rms_mode = p->rms_mode;
+      src_row = p->rms_offset + (p->rms_mode == QMLA_RMS_BF16 ? 2 : 1) * (int64_t)p->rms_heads;
+    } else {
+      return QMLA_E_INVALID;
+    }
+    dst_cols = p->rms_offset + p->rms_heads;
+  } else {
+    if (p->row_elems <= 0) return QMLA_E_INVALID;
+    a.n_copy = p->row_elems;
+    src_row = dst_cols = p->row_elems;
+  }
+  if (p->src_stride_token < src_row || p->dst_stride_row < dst_cols) return QMLA_E_INVALID;
+  a.src = reinterpret_cast<const uint8_t*>(p->src_cache);
+  a.src_sp = p->src_stride_page * se;
+  a.src_st = p->src_stride_token * se;
+  a.page_size = p->page_size;
+  a.num_pages = p->num_pages;
+  a.bt = p->block_table;
+  a.bt_stride = p->block_table_stride;
+  a.bt_cols = p->block_table_cols;
+  a.cu = p->cu_seq_lens;
+  a.t2s = p->token_to_seq;
+  a.starts = p->seq_starts;
+  a.num_seqs = p->num_seqs;
+  a.num_tokens = p->num_tokens;
+  a.dst = reinterpret_cast<uint8_t*>(p->dst);
+  a.dst_sr = p->dst_stride_row * de;
+  a.dst_dt = p->dst_dtype;
+  a.src_dt = p->src_dtype;
+  a.scale = fp8 ? p->scale : nullptr;
+  a.status = p->status;
+  // 16-byte vector path when every source and destination row starts 16-byte aligned
+  const bool vec = reinterpret_cast<uintptr_t>(a.src) % 16 == 0 && a.src_sp % 16 == 0 &&
+                   a.src_st % 16 == 0 && reinterpret_cast<uintptr_t>(a.dst) % 16 == 0 &&
+                   a.dst_sr % 16 == 0;
+  DevInfo di = dev_info(p->device);
+  if (!di.ok) return QMLA_E_CUDA;
+  // a persistent grid: as many blocks as are resident at once, each warp striding over
+  // groups of kGatherBatch rows
+  auto kern = vec ? gather_cache_kernel<true> : gather_cache_kernel<false>;
+  static std::atomic<int> resident[2];  // blocks per SM of each variant, queried once
+  int per_sm = resident[vec].load(std::memory_order_relaxed);
+  if (per_sm == 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32 * kGatherWarps, 0) !=
+            cudaSuccess ||
+        per_sm < 1)
+      per_sm = 1;
+    resident[vec].store(per_sm, std::memory_order_relaxed);
+  }
+  const int64_t rows_per_block = (int64_t)kGatherWarps * kGatherBatch;
+  const int64_t blocks = (p->num_tokens + rows_per_block - 1) / rows_per_block;
+  const int grid = (int)std::min<int64_t>(blocks, (int64_t)per_sm * di.sms);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  kern<<<grid, 32 * kGatherWarps, 0, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
 }
 

@@ -250,4 +250,200 @@ __global__ void fp8_cache_write_kernel(const __nv_bfloat16* latent, int64_t lat_
   }
 }
 
+// ---------------------------------------------------------------- prefill context gather
+// qwen_mla/ops/mla_gather.py:28-76 (gather_cache_torch).  Destination row j belongs to
+// sequence s = token_to_seq[j] and holds its token tok = j - cu_seq_lens[s] (+ seq_starts[s]),
+// found in page block_table[s][tok / page_size] at offset tok % page_size.
+//   2-byte cache: the whole row (n_copy elements) is copied, converted to the destination type.
+//   FP8 cache:    columns [0, n_e4m3) = e4m3 * scale; then rms_heads columns from rms_off
+//                 decoded from the log8 code or the raw bf16 bytes; later columns untouched.
+// One warp per destination row, 16-byte loads and stores where every row start is aligned.
+// Rows whose indices fall outside the tables are skipped and flagged in *status.
+struct GatherArgs {
+  const uint8_t* src;
+  int64_t src_sp, src_st;  // bytes per page / per token
+  int page_size, num_pages;
+  const int32_t* bt;
+  int64_t bt_stride;
+  int bt_cols;
+  const int32_t* cu;
+  const int32_t* t2s;
+  const int32_t* starts;
+  int num_seqs, num_tokens;
+  uint8_t* dst;
+  int64_t dst_sr;  // bytes per destination row
+  int dst_dt, src_dt;
+  int n_copy;                          // 2-byte cache: elements per row
+  int n_e4m3;                          // FP8 cache: e4m3 columns
+  int rms_off, rms_heads, rms_mode;    // FP8 cache: log8 / bf16-byte tail (rms_heads 0: none)
+  const float* scale;
+  int* status;
+};
+
+constexpr int kGatherWarps = 8;   // warps per block
+constexpr int kGatherBatch = 8;   // rows per warp step; lane r < 8 resolves row r's indices
+constexpr int kGatherRows = 4;    // rows whose 16-byte loads are in flight together
+constexpr int kGatherSlots = 2;   // chunks per lane per row in one pass (64 chunks of 16 B)
+
+// Streaming (evict-first) 16-byte accesses: every cache row is read once, every
+// destination row written once.
+__device__ __forceinline__ uint4 ld_stream16(const uint8_t* p) {
+  return __ldcs(reinterpret_cast<const uint4*>(p));
+}
+__device__ __forceinline__ void st_stream16(uint8_t* p, uint4 v) {
+  __stcs(reinterpret_cast<uint4*>(p), v);
+}
+
+// 16 consecutive floats to the destination type, as 16-byte stores.
+__device__ __forceinline__ void store16_vec(uint8_t* p, int dt, const float* f) {
+  if (dt == QMLA_DT_F32) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      st_stream16(p + 16 * k, make_uint4(__float_as_uint(f[4 * k]), __float_as_uint(f[4 * k + 1]),
+                                         __float_as_uint(f[4 * k + 2]), __float_as_uint(f[4 * k + 3])));
+    return;
+  }
+  uint32_t w[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    if (dt == QMLA_DT_BF16) {
+      __nv_bfloat162 b = __floats2bfloat162_rn(f[2 * k], f[2 * k + 1]);
+      w[k] = *reinterpret_cast<uint32_t*>(&b);
+    } else {
+      __half2 h = __floats2half2_rn(f[2 * k], f[2 * k + 1]);
+      w[k] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+  st_stream16(p, make_uint4(w[0], w[1], w[2], w[3]));
+  st_stream16(p + 16, make_uint4(w[4], w[5], w[6], w[7]));
+}
+
+__device__ __forceinline__ float e4m3_to_float(uint8_t b) {
+  __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)b, __NV_E4M3);
+  return __half2float(__half(h));
+}
+
+// 16 e4m3 bytes -> 16 floats, each the exact e4m3 value times sc rounded once to f32.
+__device__ __forceinline__ void e4m3x16(const uint4 v, float sc, float* f) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(
+        (__nv_fp8x2_storage_t)((w[k >> 1] >> (16 * (k & 1))) & 0xFFFFu), __NV_E4M3);
+    const float2 x = __half22float2(__half2(hr));
+    f[2 * k] = __fmul_rn(x.x, sc);
+    f[2 * k + 1] = __fmul_rn(x.y, sc);
+  }
+}
+
+// Byte offset of destination row j's source row, or -1 when its sequence, token or page
+// index falls outside the tables (mla_gather.py:41-47 index arithmetic).
+__device__ __forceinline__ int64_t gather_row_offset(const GatherArgs& a, int64_t j) {
+  const int s = __ldg(a.t2s + j);
+  if (s < 0 || s >= a.num_seqs) return -1;
+  const int64_t tok = j - (int64_t)__ldg(a.cu + s) + (a.starts ? (int64_t)__ldg(a.starts + s) : 0);
+  if (tok < 0 || tok / a.page_size >= a.bt_cols) return -1;
+  const int64_t blk = __ldg(a.bt + (int64_t)s * a.bt_stride + tok / a.page_size);
+  if (blk < 0 || blk >= a.num_pages) return -1;
+  return blk * a.src_sp + (tok % a.page_size) * a.src_st;
+}
+
+// One warp per 8 consecutive destination rows per step: lanes 0..7 resolve the rows' index
+// chains in parallel (the next step's chains are resolved while this step's loads are in
+// flight), then the 16-byte chunks of 4 rows at a time are loaded before any is stored.
+template <bool VEC>
+__global__ void __launch_bounds__(32 * kGatherWarps) gather_cache_kernel(const GatherArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int dsz = a.dst_dt == QMLA_DT_F32 ? 4 : 2;
+  const float sc = a.scale ? __ldg(a.scale) : 1.0f;
+  const bool fp8 = a.src_dt == QMLA_DT_FP8E4M3;
+  const bool same = a.dst_dt == a.src_dt;
+  const int unit = fp8 ? 16 : 8;  // columns per 16-byte source chunk
+  const int ncols = fp8 ? a.n_e4m3 : a.n_copy;
+  const int nchunk = VEC ? ncols / unit : 0;
+  const int64_t stride = (int64_t)gridDim.x * kGatherWarps * kGatherBatch;
+  int64_t base = ((int64_t)blockIdx.x * kGatherWarps + (threadIdx.x >> 5)) * kGatherBatch;
+  auto resolve = [&](int64_t b) -> int64_t {
+    int64_t off = -1;
+    if (lane < kGatherBatch && b + lane < a.num_tokens) {
+      off = gather_row_offset(a, b + lane);
+      if (off < 0 && a.status) atomicOr(a.status, QMLA_DEV_ERR_INDEX);
+    }
+    return off;
+  };
+  int64_t my = base < a.num_tokens ? resolve(base) : -1;
+  for (; base < a.num_tokens; base += stride) {
+    int64_t my_next = -1;
+#pragma unroll
+    for (int r0 = 0; r0 < kGatherBatch; r0 += kGatherRows) {
+      int64_t so[kGatherRows];
+#pragma unroll
+      for (int r = 0; r < kGatherRows; ++r) so[r] = __shfl_sync(0xffffffffu, my, r0 + r);
+      for (int cb = 0; cb < nchunk; cb += 32 * kGatherSlots) {
+        uint4 v[kGatherRows][kGatherSlots];
+#pragma unroll
+        for (int r = 0; r < kGatherRows; ++r)
+#pragma unroll
+          for (int k = 0; k < kGatherSlots; ++k) {
+            const int c = cb + 32 * k + lane;
+            v[r][k] = make_uint4(0u, 0u, 0u, 0u);
+            if (so[r] >= 0 && c < nchunk) v[r][k] = ld_stream16(a.src + so[r] + 16 * (int64_t)c);
+          }
+        if (r0 == 0 && cb == 0 && base + stride < a.num_tokens) my_next = resolve(base + stride);
+#pragma unroll
+        for (int r = 0; r < kGatherRows; ++r) {
+          uint8_t* drow = a.dst + (base + r0 + r) * a.dst_sr;
+#pragma unroll
+          for (int k = 0; k < kGatherSlots; ++k) {
+            const int c = cb + 32 * k + lane;
+            if (so[r] < 0 || c >= nchunk) continue;
+            if (fp8) {
+              float f[16];
+              e4m3x16(v[r][k], sc, f);
+              store16_vec(drow + (int64_t)c * 16 * dsz, a.dst_dt, f);
+            } else if (same) {
+              st_stream16(drow + 16 * (int64_t)c, v[r][k]);
+            } else {
+              const uint32_t w[4] = {v[r][k].x, v[r][k].y, v[r][k].z, v[r][k].w};
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const unsigned short e = (unsigned short)(w[q >> 1] >> (16 * (q & 1)));
+                const float x = a.src_dt == QMLA_DT_BF16 ? __bfloat162float(__ushort_as_bfloat16(e))
+                                                         : __half2float(__ushort_as_half(e));
+                store_from_float(drow + ((int64_t)c * 8 + q) * dsz, a.dst_dt, x);
+              }
+            }
+          }
+        }
+      }
+      if (r0 == 0 && nchunk == 0 && base + stride < a.num_tokens) my_next = resolve(base + stride);
+      // the columns the 16-byte chunks do not cover, and the FP8 rms tail
+#pragma unroll 1
+      for (int r = 0; r < kGatherRows; ++r) {
+        const int64_t off = __shfl_sync(0xffffffffu, my, r0 + r);
+        if (off < 0) continue;
+        const uint8_t* srow = a.src + off;
+        uint8_t* drow = a.dst + (base + r0 + r) * a.dst_sr;
+        for (int c = nchunk * unit + lane; c < ncols; c += 32) {
+          const float x = fp8 ? __fmul_rn(e4m3_to_float(srow[c]), sc) : load_as_float(srow + 2 * c, a.src_dt);
+          store_from_float(drow + (int64_t)c * dsz, a.dst_dt, x);
+        }
+        for (int h = lane; h < a.rms_heads; h += 32) {
+          float x;
+          if (a.rms_mode == QMLA_RMS_LOG8) {
+            // 2^(LO + code * (HI - LO) / 255), LO, HI = -3, 3, each step rounded to f32
+            x = exp2f(__fadd_rn(-3.0f, __fmul_rn((float)srow[a.rms_off + h], 6.0f / 255.0f)));
+          } else {
+            const uint16_t bits = (uint16_t)srow[a.rms_off + 2 * h] |
+                                  ((uint16_t)srow[a.rms_off + 2 * h + 1] << 8);
+            x = __bfloat162float(__ushort_as_bfloat16(bits));
+          }
+          store_from_float(drow + (int64_t)(a.rms_off + h) * dsz, a.dst_dt, x);
+        }
+      }
+    }
+    my = my_next;
+  }
+}
+
 }  // namespace qmla

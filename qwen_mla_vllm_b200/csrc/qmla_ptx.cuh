@@ -60,9 +60,11 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
   return ok != 0;
 }
 
-// Error bits written to the caller-visible status word when a wait gives up.
+// Error bits written to the caller-visible status word: a wait that gave up, or
+// (context gather) a row whose sequence, token or page index fell outside the tables.
 enum : int {
   QMLA_DEV_ERR_TIMEOUT = 1,
+  QMLA_DEV_ERR_INDEX = 2,
 };
 
 // Wait for the phase with the given parity to complete.  Gives up after

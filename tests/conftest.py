@@ -27,6 +27,33 @@ DECODE_FIXTURES = ["bf16_tp1_r768", "bf16_tp1_r256", "bf16_tp2_r384", "numerics_
                    "fp8_log8_tp2_r384"]
 
 
+GATHER_FIXTURES = ["gather_auto", "gather_log8", "gather_log8_f16", "gather_bf16", "gather_e4m3"]
+
+
+import oracle  # noqa: E402  (the checker; ROOT is on sys.path from here on)
+
+
+def to_dst_bits(x: np.ndarray, dst_dtype: str) -> np.ndarray:
+    """float32 values -> bit patterns (uint16) of the destination dtype, round to nearest even."""
+    if dst_dtype == "bfloat16":
+        return oracle.f32_to_bf16_bits(x)
+    return np.asarray(x, np.float32).astype(np.float16).view(np.uint16)
+
+
+def gather_expected(g: dict) -> np.ndarray:
+    """The destination (bit patterns) the oracle's gather writes over a 7.0-filled buffer."""
+    mode = str(g["mode"])
+    fp8 = mode != "auto"
+    vals = oracle.gather_cache(g["cache"], g["block_table"], g["cu_seq_lens"], g["token_to_seq"],
+                               int(g["num_tokens"]), fp8=fp8, scale=float(g["scale"]),
+                               seq_starts=g["seq_starts"],
+                               mla_rms=(int(g["rms_offset"]), int(g["heads"]), mode) if fp8 else None)
+    dt = str(g["dst_dtype"])
+    out = np.full(g["dst"].shape, to_dst_bits(np.float32(7.0), dt), dtype=np.uint16)
+    out[:vals.shape[0], :vals.shape[1]] = to_dst_bits(vals, dt)
+    return out
+
+
 def oracle_args(g: dict) -> dict:
     """Keyword arguments of oracle.decode for a decode fixture."""
     fp8 = str(g["kind"]) == "fp8"

@@ -3,7 +3,7 @@
 
 Run in a container where the reference plugin (sootaugur/qwen-mla-vllm) is importable:
 
-    QMLA_REFERENCE=/path/to/qwen-mla-vllm python tests/golden/make_golden.py
+    QMLA_REFERENCE=/path/to/qwen-mla-vllm python tests/golden/make_golden.py [name-prefix ...]
 
 Everything runs on the CPU.  The reference functions used (each called unmodified):
   * tests/test_fi_partial_rope.py:27-58   build / layout / ref_out   (bf16 partial-rope decode)
@@ -12,6 +12,7 @@ Everything runs on the CPU.  The reference functions used (each called unmodifie
                                           its GPU cases at import time)
   * qwen_mla/mla_impl.py:309-342          QwenMLATritonImpl.do_kv_cache_update (FP8 row writer)
   * qwen_mla/fi_decode.py:235-270         _RankPlan.plan_cpu (work-list arrays)
+  * qwen_mla/ops/mla_gather.py:28-76      gather_cache_torch (prefill context gather)
 Module-level constants the tests pin (PAGE, dev, SHUFFLE, ...) are set on the imported
 modules before the calls; shapes are kept small so the fixtures stay a few hundred KB each.
 Arrays are stored raw: bf16 as uint16 bit patterns, FP8 as uint8 bytes.
@@ -138,6 +139,49 @@ def cache_write_case(tag, mode, n=40, rank=256, packed_rope=232, heads=24, block
     print(f"{tag}: {n} tokens, width {width}")
 
 
+def gather_case(tag, mode, dst_dtype=torch.bfloat16, rank=256, rope=232, heads=24, page=16):
+    """qwen_mla/ops/mla_gather.py:28-76 on a chunk of three sequences (one empty) with
+    seq_starts, pages in random order, and sentinel-filled destination rows / columns."""
+    sys.path.insert(0, str(REF))
+    from qwen_mla.ops.mla_gather import gather_cache_torch
+    batch, ctx = 3, 100
+    g = torch.Generator().manual_seed({"auto": 21, "log8": 22, "bf16": 23, "e4m3": 24}[mode])
+    if mode == "auto":
+        pps = (ctx + page - 1) // page
+        width = rank + rope + heads
+        cache = (torch.randn(batch * pps, page, 1, width, generator=g) * 1.5).to(torch.bfloat16)
+        scale = torch.tensor(1.0)
+        mla_rms = None
+    else:
+        m = _load(REF / "tests" / "test_fp8_kv.py", "ref_fp8_kv")
+        m.PAGE, m.dev = page, torch.device("cpu")
+        lat, rp, rms, _, pps = m.make(batch, heads, ctx, rank, rope, seed=rank + heads)
+        scale = torch.tensor(float(max(lat.abs().max(), rp.abs().max())) / 448)
+        width = rank + rope + (2 if mode == "bf16" else 1) * heads
+        width += (-width) % 16
+        cache = m.fp8_cache(lat, rp, rms, scale, width, mode)
+        mla_rms = (rank + rope, heads, mode)
+    bt = torch.randperm(batch * pps, generator=g).reshape(batch, pps).to(torch.int32)
+    chunk = torch.tensor([40, 0, 57])
+    starts = torch.tensor([5, 0, 23], dtype=torch.int32)
+    cu = torch.zeros(batch + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(chunk, 0)
+    t2s = torch.repeat_interleave(torch.arange(batch, dtype=torch.int32), chunk)
+    n = int(chunk.sum())
+    dst = torch.full((n + 3, cache.shape[-1] if mode == "auto" else width), 7.0, dtype=dst_dtype)
+    gather_cache_torch(src_cache=cache, dst=dst, block_table=bt, cu_seq_lens=cu, token_to_seq=t2s,
+                       num_tokens=n, kv_cache_dtype="auto" if mode == "auto" else "fp8", scale=scale,
+                       seq_starts=starts, mla_rms=mla_rms)
+    np.savez_compressed(
+        HERE / f"{tag}.npz", mode=mode, cache=_bits(cache[:, :, 0, :]), block_table=bt.numpy(),
+        cu_seq_lens=cu.numpy(), token_to_seq=t2s.numpy(), seq_starts=starts.numpy(), num_tokens=n,
+        scale=np.float32(scale.item()), rms_offset=rank + rope, heads=heads,
+        dst_dtype=str(dst_dtype).replace("torch.", ""), dst=_bits(dst) if dst_dtype == torch.bfloat16
+        else dst.contiguous().view(torch.int16).numpy().view(np.uint16),
+        source="qwen_mla/ops/mla_gather.py:28-76")
+    print(f"{tag}: {n} rows, width {dst.shape[1]}")
+
+
 def rank_plan_case(tag, page=16):
     """fi_decode._RankPlan.plan_cpu on a stand-in object whose flashinfer wrapper records its inputs."""
     sys.path.insert(0, str(REF))
@@ -172,20 +216,33 @@ def rank_plan_case(tag, page=16):
     print(f"{tag}: {total} pages")
 
 
+CASES = {
+    "bf16_tp1_r768": lambda t: partial_rope_case(t, batch=2, heads=24, ctx=100, rank=768, rope=232),
+    "bf16_tp1_r256": lambda t: partial_rope_case(t, batch=2, heads=24, ctx=200, rank=256, rope=232),
+    "bf16_tp2_r384": lambda t: partial_rope_case(t, batch=2, heads=12, ctx=150, rank=384, rope=116),
+    "fp8_log8_r256": lambda t: fp8_case(t, batch=2, heads=24, ctx=150, rank=256, rope=232, mode="log8"),
+    "fp8_bf16_r256": lambda t: fp8_case(t, batch=2, heads=24, ctx=150, rank=256, rope=232, mode="bf16"),
+    "fp8_e4m3_r256": lambda t: fp8_case(t, batch=2, heads=24, ctx=150, rank=256, rope=232, mode="e4m3"),
+    "fp8_log8_r768": lambda t: fp8_case(t, batch=2, heads=24, ctx=100, rank=768, rope=232, mode="log8"),
+    "fp8_log8_tp2_r384": lambda t: fp8_case(t, batch=2, heads=12, ctx=130, rank=384, rope=116, mode="log8"),
+    "numerics_r256_h24": lambda t: numerics_case(t, rank=256, heads=24, ctx=100, batch=2),
+    "cache_write_log8": lambda t: cache_write_case(t, "log8"),
+    "cache_write_bf16": lambda t: cache_write_case(t, "bf16"),
+    "rank_plan": lambda t: rank_plan_case(t),
+    "gather_auto": lambda t: gather_case(t, "auto"),
+    "gather_log8": lambda t: gather_case(t, "log8"),
+    "gather_log8_f16": lambda t: gather_case(t, "log8", dst_dtype=torch.float16),
+    "gather_bf16": lambda t: gather_case(t, "bf16"),
+    "gather_e4m3": lambda t: gather_case(t, "e4m3"),
+}
+
+
 def main():
+    """Writes every fixture, or only those whose names start with one of the arguments."""
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    partial_rope_case("bf16_tp1_r768", batch=2, heads=24, ctx=100, rank=768, rope=232)
-    partial_rope_case("bf16_tp1_r256", batch=2, heads=24, ctx=200, rank=256, rope=232)
-    partial_rope_case("bf16_tp2_r384", batch=2, heads=12, ctx=150, rank=384, rope=116)
-    fp8_case("fp8_log8_r256", batch=2, heads=24, ctx=150, rank=256, rope=232, mode="log8")
-    fp8_case("fp8_bf16_r256", batch=2, heads=24, ctx=150, rank=256, rope=232, mode="bf16")
-    fp8_case("fp8_e4m3_r256", batch=2, heads=24, ctx=150, rank=256, rope=232, mode="e4m3")
-    fp8_case("fp8_log8_r768", batch=2, heads=24, ctx=100, rank=768, rope=232, mode="log8")
-    fp8_case("fp8_log8_tp2_r384", batch=2, heads=12, ctx=130, rank=384, rope=116, mode="log8")
-    numerics_case("numerics_r256_h24", rank=256, heads=24, ctx=100, batch=2)
-    cache_write_case("cache_write_log8", "log8")
-    cache_write_case("cache_write_bf16", "bf16")
-    rank_plan_case("rank_plan")
+    for tag, make in CASES.items():
+        if len(sys.argv) == 1 or any(tag.startswith(a) for a in sys.argv[1:]):
+            make(tag)
 
 
 if __name__ == "__main__":

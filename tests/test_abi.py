@@ -38,7 +38,7 @@ def test_exports_every_declared_symbol(lib):
 
 
 def test_abi_version_and_errors(lib):
-    assert lib.qmla_abi_version() == 101
+    assert lib.qmla_abi_version() == 102
     for code, text in _lib.ERRORS.items():
         assert lib.qmla_error_string(code).decode() == text
     assert lib.qmla_error_string(0).decode() == "ok"
@@ -46,7 +46,8 @@ def test_abi_version_and_errors(lib):
 
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
 @pytest.mark.parametrize("cname,pystruct", [("qmla_decode_params", _lib.DecodeParams),
-                                            ("qmla_dcp_p2p_params", _lib.DcpP2PParams)])
+                                            ("qmla_dcp_p2p_params", _lib.DcpP2PParams),
+                                            ("qmla_gather_params", _lib.GatherParams)])
 def test_params_struct_layout_matches_header(tmp_path, cname, pystruct):
     fields = [f for f, _ in pystruct._fields_]
     src = ["#include <stdio.h>", "#include <stddef.h>", '#include "qmla.h"', "int main(void) {",
@@ -71,6 +72,35 @@ def test_dcp_buffer_layout(lib):
     assert lse_off == o_off + 2 * o_slot and lse_slot == 6144
     assert total == lse_off + 2 * lse_slot
     assert lib.qmla_dcp_buffer_layout(-1, 24, 768, *[ctypes.byref(v) for v in vals]) == -1
+
+
+def test_gather_rejects_bad_arguments_without_launching(lib):
+    """Argument checks run on the host before any launch (no GPU needed)."""
+    p = _lib.GatherParams()
+    assert lib.qmla_gather_cache(None, None) == -1
+    p.num_tokens = 0
+    assert lib.qmla_gather_cache(ctypes.byref(p), None) == 0          # nothing to gather
+    p.num_tokens = -1
+    assert lib.qmla_gather_cache(ctypes.byref(p), None) == -1
+    p.num_tokens, p.num_seqs = 4, 1
+    assert lib.qmla_gather_cache(ctypes.byref(p), None) == -1         # null pointers
+    fake = 1 << 20  # never dereferenced: every call below fails its host checks first
+    p.src_cache = p.dst = p.block_table = p.cu_seq_lens = p.token_to_seq = fake
+    p.page_size, p.num_pages, p.block_table_cols = 16, 8, 4
+    p.src_dtype, p.dst_dtype = _lib.DT_F32, _lib.DT_BF16
+    assert lib.qmla_gather_cache(ctypes.byref(p), None) == -2         # f32 cache
+    p.src_dtype, p.dst_dtype = _lib.DT_FP8E4M3, _lib.DT_FP8E4M3
+    assert lib.qmla_gather_cache(ctypes.byref(p), None) == -2         # FP8 destination
+    p.dst_dtype = _lib.DT_BF16
+    p.rms_offset, p.rms_heads, p.rms_mode = 1000, 24, _lib.RMS_LOG8
+    assert lib.qmla_gather_cache(ctypes.byref(p), None) == -1         # FP8 without a scale
+    p.scale = fake
+    p.src_stride_token, p.src_stride_page, p.dst_stride_row = 1020, 16 * 1020, 1024
+    assert lib.qmla_gather_cache(ctypes.byref(p), None) == -1         # row shorter than off + heads
+    p.src_stride_token, p.src_stride_page, p.dst_stride_row = 1024, 16 * 1024, 1000
+    assert lib.qmla_gather_cache(ctypes.byref(p), None) == -1         # destination too narrow
+    p.dst_stride_row, p.rms_mode = 1024, 7
+    assert lib.qmla_gather_cache(ctypes.byref(p), None) == -1         # unknown rms mode
 
 
 def _plan(lib, lens, page):

@@ -2,7 +2,8 @@
 
 Fixtures: tests/golden/*.npz, written by tests/golden/make_golden.py from
 tests/test_fi_partial_rope.py, tests/test_fp8_kv.py, tests/test_decode_numerics.py,
-qwen_mla/mla_impl.py:do_kv_cache_update and qwen_mla/fi_decode.py:_RankPlan.plan_cpu.
+qwen_mla/mla_impl.py:do_kv_cache_update, qwen_mla/fi_decode.py:_RankPlan.plan_cpu and
+qwen_mla/ops/mla_gather.py:gather_cache_torch.
 """
 from __future__ import annotations
 
@@ -10,7 +11,7 @@ import numpy as np
 import pytest
 
 import oracle
-from conftest import DECODE_FIXTURES, load_golden, oracle_args
+from conftest import DECODE_FIXTURES, GATHER_FIXTURES, gather_expected, load_golden, oracle_args
 
 
 @pytest.mark.parametrize("name", DECODE_FIXTURES)
@@ -54,3 +55,21 @@ def test_rank_plan_arrays_exact():
     tp, indptr2, kv_len2 = oracle.plan_arrays(g["seq_lens"], int(g["page"]))
     assert np.array_equal(indptr2, g["kv_indptr"]) and np.array_equal(kv_len2, g["kv_len"])
     assert tp[-1] == sum((int(L) + oracle.TILE - 1) // oracle.TILE for L in g["seq_lens"])
+
+
+@pytest.mark.parametrize("name", GATHER_FIXTURES)
+def test_gather_bit_exact(name):
+    """Every destination element the reference's gather writes, bit for bit, and the
+    sentinel left in the rows and columns it does not write."""
+    g = load_golden(name)
+    want = g["dst"]
+    got = gather_expected(g)
+    assert np.array_equal(got, want), f"{name}: {int((got != want).sum())} elements differ"
+
+
+def test_gather_empty_and_fp8_without_layout():
+    g = load_golden("gather_log8")
+    assert oracle.gather_cache(g["cache"], g["block_table"], g["cu_seq_lens"], g["token_to_seq"], 0,
+                               fp8=True, mla_rms=(488, 24, "log8")).size == 0
+    with pytest.raises(NotImplementedError):
+        oracle.gather_cache(g["cache"], g["block_table"], g["cu_seq_lens"], g["token_to_seq"], 4, fp8=True)
