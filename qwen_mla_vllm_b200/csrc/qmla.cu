@@ -788,8 +788,40 @@ int qmla_gather_cache(const qmla_gather_params* p, void* stream) {
                    a.dst_sr % 16 == 0;
   DevInfo di = dev_info(p->device);
   if (!di.ok) return QMLA_E_CUDA;
-  // a persistent grid: as many blocks as are resident at once, each warp striding over
-  // groups of kGatherBatch rows
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // Aligned rows: the staged kernel (whole rows by the bulk-copy engine through a shared-memory
+  // ring), one block per resident slot.  Rows per stage: about 32 KB of staged bytes, 8..32.
+  BulkShape bs;
+  bs.copy_bytes = (int)(src_row / 16 * 16);
+  bs.slot = bs.copy_bytes;
+  bs.stages = 3;
+  bs.rows = bs.slot > 0 ? std::min(32, std::max(8, (32768 / std::max(bs.slot, 1)) / 8 * 8)) : 0;
+  if (const char* e = getenv("QMLA_GATHER_ROWS"))  // test hook: rows per stage (8, 16, 24, 32)
+    bs.rows = std::min(32, std::max(8, atoi(e) / 8 * 8));
+  if (const char* e = getenv("QMLA_GATHER_STAGES"))  // test hook: ring depth (2..4)
+    bs.stages = std::min(4, std::max(2, atoi(e)));
+  if (vec && bs.copy_bytes >= 16 && bulk_smem_bytes(bs) <= 200 * 1024 &&
+      getenv("QMLA_GATHER_REGS") == nullptr) {
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [] {
+      attr_err = cudaFuncSetAttribute(gather_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      kMaxDynSmem);
+    });
+    if (attr_err != cudaSuccess) return QMLA_E_CUDA;
+    const int smem = bulk_smem_bytes(bs);
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gather_bulk_kernel, kBulkThreads, smem) !=
+            cudaSuccess ||
+        per_sm < 1)
+      per_sm = 1;
+    const int64_t nbatch = (p->num_tokens + bs.rows - 1) / bs.rows;
+    const int grid = (int)std::min<int64_t>(nbatch, (int64_t)per_sm * di.sms);
+    gather_bulk_kernel<<<grid, kBulkThreads, smem, st>>>(a, bs);
+    return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
+  }
+  // Otherwise (unaligned rows, or the QMLA_GATHER_REGS test hook): register-staged loads, a
+  // persistent grid of resident blocks, each warp striding over groups of kGatherBatch rows.
   auto kern = vec ? gather_cache_kernel<true> : gather_cache_kernel<false>;
   static std::atomic<int> resident[2];  // blocks per SM of each variant, queried once
   int per_sm = resident[vec].load(std::memory_order_relaxed);
@@ -803,7 +835,6 @@ int qmla_gather_cache(const qmla_gather_params* p, void* stream) {
   const int64_t rows_per_block = (int64_t)kGatherWarps * kGatherBatch;
   const int64_t blocks = (p->num_tokens + rows_per_block - 1) / rows_per_block;
   const int grid = (int)std::min<int64_t>(blocks, (int64_t)per_sm * di.sms);
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   kern<<<grid, 32 * kGatherWarps, 0, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
 }

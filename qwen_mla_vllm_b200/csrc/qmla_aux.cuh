@@ -446,4 +446,148 @@ __global__ void __launch_bounds__(32 * kGatherWarps) gather_cache_kernel(const G
   }
 }
 
+// ---- staged variant: whole source rows through shared memory by the bulk-copy engine.
+// Warp 8 (producer) resolves one stage's 32 row indices (one lane per row) and issues one
+// cp.async.bulk per row into a ring of `stages` stages; warps 0-7 (converters) turn each
+// staged row into the destination row.  The bytes in flight no longer depend on registers:
+// stages - 1 stages per block are loading while one is converted.  Used when every row
+// start is 16-byte aligned; the bytes of a row past its last whole 16-byte unit (and of any
+// row longer than one stage slot) are read from global memory by the converters.
+constexpr int kBulkConvWarps = 8;
+constexpr int kBulkThreads = 32 * (kBulkConvWarps + 1);
+
+struct BulkShape {
+  int stages;      // ring depth, 2..4
+  int rows;        // rows per stage (multiple of 8, <= 32)
+  int slot;        // bytes per staged row (multiple of 16)
+  int copy_bytes;  // bytes bulk-copied per row (multiple of 16, <= slot)
+};
+
+__host__ __device__ inline int bulk_smem_bytes(const BulkShape& b) {
+  return b.stages * b.rows * b.slot + b.stages * b.rows * 8 + 2 * b.stages * 8 + 16;
+}
+
+__global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const GatherArgs a,
+                                                                   const BulkShape sh) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int S = sh.stages;
+  uint8_t* stage_buf = smem;
+  int64_t* row_off = reinterpret_cast<int64_t*>(smem + S * sh.rows * sh.slot);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(row_off + S * sh.rows);  // full[S], empty[S]
+  volatile int* abort_s = reinterpret_cast<volatile int*>(bars + 2 * S);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S);
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, kBulkConvWarps);
+    }
+    *abort_s = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int64_t nbatch = (a.num_tokens + sh.rows - 1) / sh.rows;
+  if (warp == kBulkConvWarps) {
+    // ---- producer
+    const uint64_t pol = policy_evict_first();
+    int i = 0;
+    for (int64_t batch = blockIdx.x; batch < nbatch; batch += gridDim.x, ++i) {
+      const int st = i % S;
+      if (i >= S &&
+          !mbar_wait(empty0 + 8 * st, (uint32_t)((i / S - 1) & 1), abort_s, a.status))
+        break;
+      const int64_t row = batch * sh.rows + lane;
+      int64_t off = -1;
+      if (lane < sh.rows && row < a.num_tokens) {
+        off = gather_row_offset(a, row);
+        if (off < 0 && a.status) atomicOr(a.status, QMLA_DEV_ERR_INDEX);
+      }
+      if (lane < sh.rows) row_off[st * sh.rows + lane] = off;
+      const uint32_t mine = off >= 0 ? (uint32_t)sh.copy_bytes : 0u;
+      const uint32_t total = __reduce_add_sync(0xffffffffu, mine);
+      __syncwarp();
+      if (lane == 0) mbar_expect_tx(full0 + 8 * st, total);  // the arrive publishes row_off
+      __syncwarp();
+      if (mine)
+        bulk_load_1d(smem_u32(stage_buf + (st * sh.rows + lane) * sh.slot), a.src + off, mine,
+                     full0 + 8 * st, pol);
+    }
+    // wait (bounded) until the copies of the last uses of every stage have landed, so that
+    // none is in flight when the block exits
+    const int issued = i;
+    for (int u = issued - 1; u >= 0 && u >= issued - S; --u) {
+      const int st = u % S;
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(full0 + 8 * st, (uint32_t)((u / S) & 1)) &&
+             globaltimer_ns() - t0 < 2000000000ull) {
+      }
+    }
+    return;
+  }
+  // ---- converters: warp w takes rows w, w + 8, ... of each stage
+  const int dsz = a.dst_dt == QMLA_DT_F32 ? 4 : 2;
+  const float sc = a.scale ? __ldg(a.scale) : 1.0f;
+  const bool fp8 = a.src_dt == QMLA_DT_FP8E4M3;
+  const bool same = a.dst_dt == a.src_dt;
+  const int unit = fp8 ? 16 : 8;
+  const int ncols = fp8 ? a.n_e4m3 : a.n_copy;
+  const int nchunk = min(ncols / unit, sh.copy_bytes / 16);  // chunks wholly inside the staged bytes
+  int i = 0;
+  for (int64_t batch = blockIdx.x; batch < nbatch; batch += gridDim.x, ++i) {
+    const int st = i % S;
+    if (!mbar_wait(full0 + 8 * st, (uint32_t)((i / S) & 1), abort_s, a.status)) break;
+    for (int r = warp; r < sh.rows; r += kBulkConvWarps) {
+      const int64_t off = row_off[st * sh.rows + r];
+      if (off < 0) continue;
+      const uint8_t* ss = stage_buf + (st * sh.rows + r) * sh.slot;
+      const uint8_t* sg = a.src + off;
+      uint8_t* drow = a.dst + (batch * sh.rows + r) * a.dst_sr;
+      for (int c = lane; c < nchunk; c += 32) {
+        const uint4 v = *reinterpret_cast<const uint4*>(ss + 16 * c);
+        if (fp8) {
+          float f[16];
+          e4m3x16(v, sc, f);
+          store16_vec(drow + (int64_t)c * 16 * dsz, a.dst_dt, f);
+        } else if (same) {
+          st_stream16(drow + 16 * (int64_t)c, v);
+        } else {
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const unsigned short e = (unsigned short)(w[q >> 1] >> (16 * (q & 1)));
+            const float x = a.src_dt == QMLA_DT_BF16 ? __bfloat162float(__ushort_as_bfloat16(e))
+                                                     : __half2float(__ushort_as_half(e));
+            store_from_float(drow + ((int64_t)c * 8 + q) * dsz, a.dst_dt, x);
+          }
+        }
+      }
+      auto byte_at = [&](int b) -> uint8_t { return b < sh.copy_bytes ? ss[b] : sg[b]; };
+      for (int c = nchunk * unit + lane; c < ncols; c += 32) {
+        float x;
+        if (fp8) {
+          x = __fmul_rn(e4m3_to_float(byte_at(c)), sc);
+        } else {
+          const unsigned short e = (unsigned short)(byte_at(2 * c) | (byte_at(2 * c + 1) << 8));
+          x = a.src_dt == QMLA_DT_BF16 ? __bfloat162float(__ushort_as_bfloat16(e))
+                                       : __half2float(__ushort_as_half(e));
+        }
+        store_from_float(drow + (int64_t)c * dsz, a.dst_dt, x);
+      }
+      for (int h = lane; h < a.rms_heads; h += 32) {
+        float x;
+        if (a.rms_mode == QMLA_RMS_LOG8) {
+          x = exp2f(__fadd_rn(-3.0f, __fmul_rn((float)byte_at(a.rms_off + h), 6.0f / 255.0f)));
+        } else {
+          const uint16_t bits = (uint16_t)byte_at(a.rms_off + 2 * h) |
+                                ((uint16_t)byte_at(a.rms_off + 2 * h + 1) << 8);
+          x = __bfloat162float(__ushort_as_bfloat16(bits));
+        }
+        store_from_float(drow + (int64_t)(a.rms_off + h) * dsz, a.dst_dt, x);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty0 + 8 * st);
+  }
+}
+
 }  // namespace qmla

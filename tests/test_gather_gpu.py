@@ -82,12 +82,18 @@ def _chunk(rng, n_seqs, P, page, max_len):
 
 @pytest.mark.parametrize("mode", ["log8", "bf16", "e4m3"])
 @pytest.mark.parametrize("dst_dt", ["bfloat16", "float16"])
-@pytest.mark.parametrize("aligned", [True, False])
-def test_gather_fp8_config_shapes(cuda_device, mode, dst_dt, aligned):
-    """rank 768 + rope 232, 24 heads (the TP=1 row); aligned rows take the 16-byte path,
-    a 1030-byte row stride and an odd destination offset take the scalar path."""
+@pytest.mark.parametrize("path", ["bulk", "regs", "scalar"])
+def test_gather_fp8_config_shapes(cuda_device, monkeypatch, mode, dst_dt, path):
+    """rank 768 + rope 232, 24 heads (the TP=1 row).  Aligned rows take the staged kernel
+    (bulk copies through shared memory) or, with the QMLA_GATHER_REGS hook, the
+    register-staged 16-byte path; a 1030-byte row stride and an odd destination offset take
+    the scalar path."""
     from qwen_mla_vllm_b200.mla_gather import gather_cache_torch
-    rng = np.random.default_rng(["log8", "bf16", "e4m3"].index(mode) * 4 + (dst_dt == "float16") * 2 + aligned)
+    if path == "regs":
+        monkeypatch.setenv("QMLA_GATHER_REGS", "1")
+    aligned = path != "scalar"
+    rng = np.random.default_rng(["log8", "bf16", "e4m3"].index(mode) * 8 + (dst_dt == "float16") * 4 +
+                                ["bulk", "regs", "scalar"].index(path))
     off, nh, page, P = 1000, 24, 16, 96
     width = (1056 if mode == "bf16" else 1024) if aligned else 1030 + (24 if mode == "bf16" else 0)
     rows = _fp8_case(rng, P, page, off, nh, mode, width)
@@ -110,6 +116,29 @@ def test_gather_fp8_config_shapes(cuda_device, mode, dst_dt, aligned):
     exp = np.full(got.shape, to_dst_bits(np.float32(5.0), dst_dt), np.uint16)
     exp[:n, :off + nh] = to_dst_bits(want, dst_dt)
     assert np.array_equal(got, exp), f"{int((got != exp).sum())} elements differ"
+
+
+@pytest.mark.parametrize("mode", ["log8", "bf16"])
+def test_gather_fp8_wide_rows(cuda_device, mode):
+    """rank 1792 + rope 232 (rows of 2 KB and more: 16 and 8 rows per stage); a chunk
+    whose row count is not a multiple of the stage's."""
+    from qwen_mla_vllm_b200.mla_gather import gather_cache_torch
+    rng = np.random.default_rng(17 + (mode == "bf16"))
+    off, nh, page, P = 2024, 24, 16, 48
+    width = 2048 if mode == "log8" else 2080
+    rows = _fp8_case(rng, P, page, off, nh, mode, width)
+    bt, cu, t2s, starts, n = _chunk(rng, 5, P, page, 333)
+    want = oracle.gather_cache(rows, bt, cu, t2s, n, fp8=True, scale=0.25, seq_starts=starts,
+                               mla_rms=(off, nh, mode))
+    dst = torch.full((n, off + nh), 5.0, dtype=torch.bfloat16, device=cuda_device)
+    gather_cache_torch(src_cache=torch.from_numpy(rows).to(cuda_device).view(torch.float8_e4m3fn).unsqueeze(2),
+                       dst=dst, block_table=torch.from_numpy(bt).to(cuda_device),
+                       cu_seq_lens=torch.from_numpy(cu).to(cuda_device),
+                       token_to_seq=torch.from_numpy(t2s).to(cuda_device), num_tokens=n, kv_cache_dtype="fp8",
+                       scale=torch.tensor(0.25, device=cuda_device),
+                       seq_starts=torch.from_numpy(starts).to(cuda_device), mla_rms=(off, nh, mode), check=True)
+    got = _bits(dst)
+    assert np.array_equal(got, to_dst_bits(want, "bfloat16"))
 
 
 def test_gather_fp8_log8_f32_destination(cuda_device):
