@@ -457,7 +457,7 @@ constexpr int kBulkConvWarps = 8;
 constexpr int kBulkThreads = 32 * (kBulkConvWarps + 1);
 
 struct BulkShape {
-  int stages;      // ring depth, 2..4
+  int stages;      // ring depth, 2..8
   int rows;        // rows per stage (multiple of 8, <= 32)
   int slot;        // bytes per staged row (multiple of 16)
   int copy_bytes;  // bytes bulk-copied per row (multiple of 16, <= slot)
