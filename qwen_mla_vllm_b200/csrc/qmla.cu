@@ -794,10 +794,12 @@ int qmla_gather_cache(const qmla_gather_params* p, void* stream) {
   BulkShape bs;
   bs.copy_bytes = (int)(src_row / 16 * 16);
   bs.slot = bs.copy_bytes;
-  // 8 rows per stage, 4 stages: small stages let up to 7 blocks share an SM (swept on the FP8
-  // log8 bench shape: 4.82 TB/s against 4.58 for 32 rows x 3 stages)
-  bs.stages = 4;
-  bs.rows = 8;
+  // A 6-deep ring of 16 rows (8 when 16 would take more than ~100 KB of shared memory).  Swept
+  // on the FP8 log8 bench shape: 16 x 6 gave 4.96 TB/s, 8 x 6 4.91, 8 x 4 4.73-4.82,
+  // 32 x 3 4.58; a deeper ring counted for more than more blocks per SM.
+  bs.stages = 6;
+  bs.rows = 16;
+  if (bulk_smem_bytes(bs) > 100 * 1024) bs.rows = 8;
   if (const char* e = getenv("QMLA_GATHER_ROWS"))  // test hook: rows per stage (8, 16, 24, 32)
     bs.rows = std::min(32, std::max(8, atoi(e) / 8 * 8));
   if (const char* e = getenv("QMLA_GATHER_STAGES"))  // test hook: ring depth (2..8)
