@@ -242,6 +242,7 @@ GATHER_SEQS, GATHER_LEN = 16, 8192
 GATHER_WORKLOAD = ("prefill context gather: FP8-e4m3 cache rows (768|232 e4m3 + 24 log8 codes, 1024 B) "
                    "-> bf16 [131072, 1024], 16 sequences x 8192 tokens, 16-token pages in random order")
 GATHER_METRIC = "MLA prefill context gather achieved HBM GB/s (FP8 -> bf16 dequant)"
+GATHER_TRAFFIC = 344.8e6  # dram__bytes of the default kernel's ncu launch (profiles/gather_fp8_log8_131k.md)
 
 
 def gather_row_bytes() -> float:
@@ -354,8 +355,11 @@ def run_gather(args) -> None:
         "config": {"workload": GATHER_WORKLOAD, "rows": n, "row_bytes_read": ROW, "dst_bytes_per_row": 2 * ROW,
                    "l2": f"inputs larger than L2 ({n * gather_row_bytes() / 1e6:.0f} MB moved per step), no flush"},
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
-                     "traffic": None, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                     "kernel": "gather_cache_kernel (one launch per step)"},
+                     "traffic": GATHER_TRAFFIC,
+                     "traffic_note": "dram bytes of one cold ncu launch (profiles/gather_fp8_log8_131k.md); "
+                                     "part of the cache was still in L2 and part of the writes still dirty",
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                     "kernel": "gather_bulk_kernel (one launch per step)"},
         "cpu_baseline": cpu,
         "e2e": {"value": total / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
