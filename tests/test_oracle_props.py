@@ -1,5 +1,6 @@
 """Properties of the oracle that need no reference fixture: number formats against torch's
-own conversions, MTP flattening, and DCP split-and-merge consistency."""
+own conversions, MTP flattening, DCP split-and-merge consistency, and the FP8 writer / context
+gather round trip."""
 from __future__ import annotations
 
 import numpy as np
@@ -116,3 +117,57 @@ def test_plan_arrays_edge_cases():
     assert tp.tolist() == [0, 0, 0, 1, 2, 3, 4]
     assert indptr.tolist() == [0, 0, 0, 1, 5, 10, 18]
     assert kv_len.tolist() == [0, 0, 1, 64, 65, 128]
+
+
+def test_log8_decode_bf16_f16_rounding_margin():
+    """The gather's bit-exact claim for bf16 / f16 destinations: for every log8 code, the exact
+    2^(fl(-3 + fl(code * fl(6/255)))) lies more than 40 float32 ulps from the nearest bf16 /
+    f16 rounding midpoint, so any exp2 within a few ulps rounds to the same destination value."""
+    import math
+    c = np.arange(256, dtype=np.float32)
+    x = (np.float32(-3.0) + (c * np.float32(6.0 / 255.0)).astype(np.float32)).astype(np.float32)
+    for mant_bits, need in ((7, 150), (10, 40)):
+        worst = math.inf
+        for v in x:
+            e = 2.0 ** float(v)
+            _, ex = math.frexp(e)
+            step = 2.0 ** (ex - 1 - mant_bits)
+            mid = (math.floor(e / step) + 0.5) * step
+            worst = min(worst, abs(e - mid) / 2.0 ** (ex - 24))
+        assert worst > need, (mant_bits, worst)
+
+
+@pytest.mark.parametrize("mode", ["log8", "bf16"])
+def test_cache_write_then_gather_round_trip(mode):
+    """Rows written by the FP8 writer (mla_impl.py:309-342) and gathered back
+    (ops/mla_gather.py:28-76) give e4m3(x / k_scale) * k_scale and the rms decode, for a chunk
+    whose sequences start mid-page."""
+    rng = np.random.default_rng(8)
+    rank, rope, heads, page = 256, 232, 24, 16
+    n_tok = 40 * page
+    lat = oracle.bf16_round(rng.standard_normal((n_tok, rank)).astype(np.float32) * 2)
+    kpe = np.concatenate([oracle.bf16_round(rng.standard_normal((n_tok, rope)).astype(np.float32)),
+                          oracle.bf16_round(np.exp(rng.standard_normal((n_tok, heads)) * 0.6).astype(np.float32))], 1)
+    ks = float(np.abs(lat).max()) / 448
+    rows = oracle.fp8_cache_rows(lat, kpe, ks, rope, heads, mode)
+    W = rows.shape[1] + (-rows.shape[1]) % 16
+    cache = np.zeros((n_tok, W), np.uint8)
+    perm = rng.permutation(40)                  # token t lives in page perm[t // page]
+    slots = perm[np.arange(n_tok) // page] * page + np.arange(n_tok) % page
+    cache[slots, :rows.shape[1]] = rows
+    cache = cache.reshape(40, page, W)
+    bt = np.stack([perm[:20], perm[20:]]).astype(np.int32)       # two sequences of 320 tokens
+    starts = np.array([17, 100], np.int32)
+    lens = np.array([300, 220])
+    cu = np.array([0, 300, 520], np.int32)
+    t2s = np.repeat(np.arange(2, dtype=np.int32), lens)
+    got = oracle.gather_cache(cache, bt, cu, t2s, 520, fp8=True, scale=ks, seq_starts=starts,
+                              mla_rms=(rank + rope, heads, mode))
+    tok = np.concatenate([np.arange(17, 317), 320 + np.arange(100, 320)])
+    x = np.concatenate([lat, kpe[:, :rope]], 1)[tok]
+    inv = np.float32(1.0) / np.float32(ks)     # the writer multiplies by 1 / k_scale (mla_impl.py:329-332)
+    want_lat = oracle.e4m3_decode(oracle.e4m3_encode(np.clip(x * inv, -448, 448))) * np.float32(ks)
+    assert np.array_equal(got[:, :rank + rope], want_lat.astype(np.float32))
+    r = kpe[tok, rope:]
+    want_rms = oracle.log8_decode(oracle.log8_encode(r)) if mode == "log8" else r
+    assert np.array_equal(got[:, rank + rope:], want_rms)
