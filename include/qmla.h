@@ -205,7 +205,11 @@ int qmla_fp8_cache_write(const void* latent, int64_t latent_stride, const void* 
  *     head, 2^(-3 + code * 6/255)), QMLA_RMS_BF16 (two raw bf16 bytes per head) or
  *     QMLA_RMS_NATIVE (e4m3 * scale, like the latent).  Later columns are untouched.
  * Rows whose sequence, token or page index falls outside the tables are skipped and
- * set bit 2 of *status (when status is not NULL). */
+ * OR QMLA_STATUS_BAD_INDEX into *status (when status is not NULL); a wait of the
+ * staged variant that gives up ORs QMLA_STATUS_TIMEOUT.  Neither happens on valid
+ * tables. */
+#define QMLA_STATUS_TIMEOUT 1   /* a device wait gave up (every kernel with waits) */
+#define QMLA_STATUS_BAD_INDEX 2 /* context gather: a row's index fell outside the tables */
 typedef struct qmla_gather_params {
   const void* src_cache;                    /* element (p, t, c) at p*stride_page + t*stride_token + c */
   int64_t src_stride_page, src_stride_token; /* elements of src_dtype */
@@ -224,7 +228,7 @@ typedef struct qmla_gather_params {
   void* dst;                                /* [num_tokens][dst_stride_row] */
   int64_t dst_stride_row;                   /* elements of dst_dtype */
   int32_t dst_dtype;                        /* QMLA_DT_BF16, QMLA_DT_F16 or QMLA_DT_F32 */
-  int32_t* status;                          /* optional device word; bit 2 = bad index */
+  int32_t* status;                          /* optional device word (QMLA_STATUS_* bits) */
   int32_t device;
 } qmla_gather_params;
 

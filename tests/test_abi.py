@@ -151,3 +151,10 @@ def test_launching_entry_points_validate_before_touching_cuda(lib):
     assert lib.qmla_dcp_merge(None, 2, None, None, 0, None, 2, 1, 1, 1, None) == -1
     assert lib.qmla_dcp_correct(None, 2, 0, 0, None, 0, 0, None, 2, 0, 1, 1, 1, 1, None) == -1
     assert lib.qmla_fp8_cache_write(None, 0, None, 0, None, 1, 1, 1, 1, 3, None, None, 1, None) == -1
+
+
+def test_status_bits_match_binding():
+    """QMLA_STATUS_* in qmla.h are the bits the Python binding tests for."""
+    bits = dict(re.findall(r"#define QMLA_STATUS_(\w+) (\d+)", HEADER.read_text()))
+    assert int(bits["TIMEOUT"]) == _lib.DEV_ERR_TIMEOUT
+    assert int(bits["BAD_INDEX"]) == _lib.DEV_ERR_INDEX
