@@ -4,8 +4,10 @@
  * C ABI of libqmla.so.  Plain pointers and sizes only; every device pointer is
  * a CUDA device address, `stream` is a cudaStream_t passed as void*.  No entry
  * point allocates device memory or synchronises the device (the qmla_dcp_buffer_*
- * set-up calls and the two status readers excepted), so the launching entry
- * points may be recorded into a CUDA graph.
+ * set-up calls and the status readers excepted).  qmla_mla_decode, the DCP and
+ * cache-writer kernels and the context gather may be recorded into a CUDA graph.
+ * Entry points that take a `device` make it current for the call and restore the
+ * caller's current device before they return.
  * Host-side the library keeps only per-device attributes and a small cache of
  * TMA descriptors.  Entry points return 0 on success or a negative QMLA_E_*
  * code.
@@ -135,13 +137,27 @@ int qmla_decode_workspace_bytes(const qmla_decode_params* p, int64_t* bytes);
  * kernel on `stream`. */
 int qmla_mla_decode(const qmla_decode_params* p, void* stream);
 
-/* qmla_mla_decode without a caller workspace (no reference counterpart: the reference's
- * decode always receives vLLM-owned scratch).  Uses a 32 MiB device array inside the library
- * (one per device, its address looked up once); shapes whose workspace would exceed it return
- * QMLA_E_WORKSPACE.  No device memory is allocated.  Calls on one device share that array:
- * two calls whose executions overlap (different streams, or graphs replayed concurrently)
- * race on it, so callers must order them (one stream, or events). */
+/* qmla_mla_decode for callers that cannot allocate device memory.  No counterpart in the
+ * reference: its decode always receives scratch that vLLM's workspace manager owns.  Here the
+ * callers are hosts that reach this library through a foreign-function layer that hands over
+ * only the input and output buffers (no device allocator, nowhere to keep a workspace between
+ * calls), and serving processes whose device memory pool is sized and locked at start-up, where
+ * a later cudaMalloc would fail.  The call ignores p->workspace and uses a 32 MiB device array
+ * inside the library instead; it calls no cudaMalloc, cudaFree or other allocating routine.
+ *  - Limit: shapes whose qmla_decode_workspace_bytes() exceeds 32 MiB return QMLA_E_WORKSPACE
+ *    before anything is launched (about 513,000 rows at 160 CTAs x 32 heads x rank 768).
+ *  - Every GPU that loads the library holds one such array until the process exits.  The first
+ *    call on a device looks up the array's device address (cudaGetSymbolAddress) with that
+ *    device current; make that first call before any stream capture.
+ *  - Every call on a device shares its array, which keeps the last call's contents (the status
+ *    word is cleared by each call).  Two calls whose executions overlap on the GPU (different
+ *    streams, or concurrent graph replays) race on it: order them on one stream or with events.
+ *  - qmla_static_read_status reads the status word of the last static call on a device. */
 int qmla_mla_decode_static(const qmla_decode_params* p, void* stream);
+
+/* Status word of the last qmla_mla_decode_static call on `device` (same bits as
+ * qmla_read_status).  Copies 4 bytes device->host on `stream` and synchronises that stream. */
+int qmla_static_read_status(int32_t device, void* stream, int32_t* status);
 
 /* Device status word of the last call that used `workspace`: 0, or bit 0 set
  * when a kernel wait timed out.  Copies 4 bytes device->host on `stream` and

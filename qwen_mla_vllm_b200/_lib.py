@@ -152,6 +152,7 @@ PROTOTYPES = {
     "qmla_mla_decode": (ctypes.c_int, [ctypes.POINTER(DecodeParams), _VP]),
     "qmla_mla_decode_static": (ctypes.c_int, [ctypes.POINTER(DecodeParams), _VP]),
     "qmla_read_status": (ctypes.c_int, [_VP, _VP, ctypes.POINTER(_I32)]),
+    "qmla_static_read_status": (ctypes.c_int, [_I32, _VP, ctypes.POINTER(_I32)]),
     "qmla_plan": (ctypes.c_int, [_VP, _I32, _I32, _VP, _VP, _VP, ctypes.POINTER(_I64), ctypes.POINTER(_I64)]),
     "qmla_dcp_correct": (ctypes.c_int, [_VP, _I32, _I64, _I64, _VP, _I64, _I64, _VP, _I32, _I32, _I32,
                                         _I32, _I32, _I32, _VP]),

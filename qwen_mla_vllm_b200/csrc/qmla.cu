@@ -131,6 +131,32 @@ int gcd_int(int a, int b) {
 
 int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
+// Makes `dev` the current device for the lifetime of the guard and puts the caller's current
+// device back on every return path, so an entry point never leaves a thread that drives several
+// GPUs pointed at another one.
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev_) != cudaSuccess) return;
+    if (prev_ == dev) {
+      ok_ = true;
+      return;
+    }
+    ok_ = cudaSetDevice(dev) == cudaSuccess;
+    switched_ = ok_;
+  }
+  ~DeviceGuard() {
+    if (switched_) cudaSetDevice(prev_);
+  }
+  bool ok() const { return ok_; }
+  DeviceGuard(const DeviceGuard&) = delete;
+  DeviceGuard& operator=(const DeviceGuard&) = delete;
+
+ private:
+  int prev_ = -1;
+  bool ok_ = false, switched_ = false;
+};
+
 struct Plan {
   int npv, nb, nqk;
   int use_tma, run;
@@ -354,8 +380,10 @@ unsigned long long* g_trace = nullptr;
 #endif
 
 // Scratch for qmla_mla_decode_static: a fixed device array instead of a caller workspace.
-// 32 MiB covers the decode workspace up to 160 CTAs x 32 heads x rank 768 (31.5 MB of fp32
-// partials) with up to 16383 rows.  One array per device, shared by every call on it.
+// A call fits when qmla_decode_workspace_bytes() <= 32 MiB.  The per-CTA fp32 partials take the
+// most: at the largest shape (160 CTAs x 32 heads x rank 768, 31.5 MB of partials) about 513,000
+// rows still fit; at one CTA per B200 SM with 24 heads and rank 768, about 2.9 million.  Every GPU
+// that loads the library holds one copy until the process exits, shared by every call on it.
 constexpr int64_t kStaticScratchBytes = int64_t(32) << 20;
 __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
 std::map<int, void*> g_static_addr;  // device -> address of g_static_scratch (looked up once)
@@ -379,7 +407,7 @@ extern "C" {
 void qmla_set_trace(void* dev_ptr) { g_trace = reinterpret_cast<unsigned long long*>(dev_ptr); }
 #endif
 
-int qmla_abi_version(void) { return 102; }
+int qmla_abi_version(void) { return 103; }
 
 const char* qmla_error_string(int code) {
   switch (code) {
@@ -418,9 +446,8 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
   if (!p->workspace || p->workspace_bytes < pl.ws_total) return QMLA_E_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(p->workspace) % 256 != 0) return QMLA_E_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  int cur = -1;
-  if (cudaGetDevice(&cur) != cudaSuccess) return QMLA_E_CUDA;
-  if (cur != p->device && cudaSetDevice(p->device) != cudaSuccess) return QMLA_E_CUDA;
+  DeviceGuard dg(p->device);
+  if (!dg.ok()) return QMLA_E_CUDA;
 
   uint8_t* ws = reinterpret_cast<uint8_t*>(p->workspace);
   DecodeArgs a;
@@ -529,17 +556,26 @@ int qmla_mla_decode_static(const qmla_decode_params* p, void* stream) {
   int rc = qmla_decode_workspace_bytes(p, &need);
   if (rc != QMLA_OK) return rc;
   if (need > kStaticScratchBytes) return QMLA_E_WORKSPACE;
-  int cur = -1;
-  if (cudaGetDevice(&cur) != cudaSuccess) return QMLA_E_CUDA;
-  if (cur != p->device && cudaSetDevice(p->device) != cudaSuccess) return QMLA_E_CUDA;
+  DeviceGuard dg(p->device);
+  if (!dg.ok()) return QMLA_E_CUDA;
   void* scratch = static_scratch(p->device);
   if (!scratch) return QMLA_E_CUDA;
-  // Same launch sequence as qmla_mla_decode; its plan kernel (or the memset taken with a
-  // precomputed plan) clears the status word, the only scratch that must start at zero.
+  // Same launch sequence as qmla_mla_decode.  The status word is the only scratch that must
+  // start at zero: plan_kernel clears it, or bounds_kernel when a precomputed plan is given.
+  // Everything else a call reads from the array it has written earlier in the same call.
   qmla_decode_params q = *p;
   q.workspace = scratch;
   q.workspace_bytes = kStaticScratchBytes;
   return qmla_mla_decode(&q, stream);
+}
+
+int qmla_static_read_status(int32_t device, void* stream, int32_t* status) {
+  if (!status) return QMLA_E_INVALID;
+  DeviceGuard dg(device);
+  if (!dg.ok()) return QMLA_E_CUDA;
+  void* scratch = static_scratch(device);
+  if (!scratch) return QMLA_E_CUDA;
+  return qmla_read_status(scratch, stream, status);
 }
 
 int qmla_read_status(const void* workspace, void* stream, int32_t* status) {

@@ -38,7 +38,7 @@ def test_exports_every_declared_symbol(lib):
 
 
 def test_abi_version_and_errors(lib):
-    assert lib.qmla_abi_version() == 102
+    assert lib.qmla_abi_version() == 103
     for code, text in _lib.ERRORS.items():
         assert lib.qmla_error_string(code).decode() == text
     assert lib.qmla_error_string(0).decode() == "ok"

@@ -289,3 +289,33 @@ def test_cuda_graph_replay(cuda_device):
     torch.cuda.synchronize()
     assert torch.equal(o, want_o) and torch.equal(lse, want_lse)
     del graph
+
+
+def test_entry_points_restore_current_device(cuda_device):
+    """qmla_mla_decode and qmla_mla_decode_static make p->device current for the call only: a
+    thread whose current device is another GPU keeps it (needs a second GPU)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import ctypes
+    from qwen_mla_vllm_b200 import _lib
+    from qwen_mla_vllm_b200.mla_decode_attention import build_params, run_params
+    lens = [300, 65]
+    cache, q, bt, sl = make_bf16_case(len(lens), 24, 768, 232, 16, lens, seed=3, device=cuda_device)
+    o = torch.zeros(2, 24, 768, dtype=torch.bfloat16, device=cuda_device)
+    p = build_params(q, cache, o, None, bt, sl, rank=768, qk_dim=1000, rms_offset=1000, rms_mode=1,
+                     page_size=16, sm_scale=1 / 16)
+    run_params(p, cuda_device)  # sizes and attaches a workspace on device 0
+    torch.cuda.synchronize(cuda_device)
+    lib = _lib.load()
+    stream0 = torch.cuda.current_stream(cuda_device).cuda_stream
+    prev = torch.cuda.current_device()
+    try:
+        torch.cuda.set_device(1)
+        for fn in (lib.qmla_mla_decode, lib.qmla_mla_decode_static):
+            _lib.check(fn.__name__, fn(ctypes.byref(p), ctypes.c_void_p(stream0)))
+            assert torch.cuda.current_device() == 1
+        torch.cuda.synchronize(cuda_device)
+    finally:
+        torch.cuda.set_device(prev)
+    ref_o, _ = oracle_ref(q, cache, bt, sl, rank=768, qk_dim=1000, page=16, sm_scale=1 / 16, rms_offset=1000)
+    compare(o, None, ref_o, None, tol=BF16_TOL)

@@ -1,6 +1,10 @@
-"""qmla_mla_decode_static (the no-workspace entry point) against qmla_mla_decode on the same
-inputs: two consecutive calls, bit-identical outputs.  Collected last (file name) so it also
-runs after every other GPU test has used the library."""
+"""qmla_mla_decode_static, the decode entry point for callers that cannot allocate device memory
+(hosts that reach the library through a foreign-function layer with no device allocator, and
+serving processes whose memory pool is locked at start-up).  It runs on a fixed array inside the
+library instead of a caller workspace.  Checked against qmla_mla_decode on the same inputs: two
+consecutive calls, bit-identical outputs, a clear status word, and the oversize refusal.  Collected
+last (file name), so it also runs after every other GPU test has used the library; it passes alone
+in a fresh process too."""
 from __future__ import annotations
 
 import ctypes
@@ -17,6 +21,15 @@ def _static_call(p, device):
     from qwen_mla_vllm_b200 import _lib
     stream = torch.cuda.current_stream(device).cuda_stream
     _lib.check("qmla_mla_decode_static", _lib.load().qmla_mla_decode_static(ctypes.byref(p), ctypes.c_void_p(stream)))
+
+
+def _static_status(device):
+    from qwen_mla_vllm_b200 import _lib
+    st = ctypes.c_int32(-1)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    _lib.check("qmla_static_read_status",
+               _lib.load().qmla_static_read_status(device.index or 0, ctypes.c_void_p(stream), ctypes.byref(st)))
+    return st.value
 
 
 @pytest.mark.parametrize("fp8", [False, True])
@@ -47,6 +60,7 @@ def test_static_scratch_matches_workspace_entry_point(cuda_device, fp8):
         torch.cuda.synchronize()
         assert torch.equal(o, o_ref)
         assert torch.equal(l, l_ref)
+        assert _static_status(cuda_device) == 0  # no device wait gave up
 
 
 def test_static_scratch_rejects_oversize(cuda_device):
