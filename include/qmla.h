@@ -252,14 +252,21 @@ int qmla_gather_cache(const qmla_gather_params* p, void* stream);
 
 /* ---- DCP over NVLink peer memory ------------------------------------------
  * Each rank of a DCP group (one process per GPU) owns one exchange buffer:
- *   [header 256 B: flags[8] u32 (epoch published by each rank), status u32]
+ *   [header 256 B: flags[8] u32 (epoch published by each rank), status u32 at byte 32,
+ *    last merged epoch u32 at byte 36 and a block counter u32 at byte 40 (device-epoch mode),
+ *    merge stats u64[3] at byte 64 (merges, ns spent waiting for the peers' flags, ns from
+ *    entry to exit; block 0 of each qmla_dcp_p2p_merge adds to them; the host may zero them)]
  *   [o partial, 2 slots of B*H*D f32, each 256-B aligned]
  *   [lse partial, 2 slots of B*H f32 (natural log), each 256-B aligned]
  * qmla_dcp_buffer_layout returns the byte offsets.  A decode step e writes the
  * rank's partial into slot e&1 of its own buffer (qmla_mla_decode with o / lse
  * pointing there, f32 o); qmla_dcp_p2p_merge(epoch = e) then merges all ranks'
  * slot-e&1 partials, reading the peers' buffers through their IPC mappings.
- * Epochs start at 1 and grow by one per step on every rank. */
+ * Epochs start at 1 and grow by one per step on every rank.  With epoch = 0 the kernel
+ * takes the epoch from the device instead (one past the last epoch this rank merged, kept in
+ * its header and advanced by the merge itself), so a captured CUDA graph can be replayed; a
+ * captured sequence then needs an even number of merges per replay so each replay starts on
+ * the same slot.  A group uses one mode for its whole life. */
 #define QMLA_DCP_MAX_WORLD 8
 #define QMLA_DCP_ALL_HEADS 0     /* every rank gets o[B, H, D] */
 #define QMLA_DCP_HEAD_SCATTER 1  /* rank r gets heads [r*H/world, (r+1)*H/world): o[B, H/world, D] */
@@ -281,7 +288,7 @@ typedef struct qmla_dcp_p2p_params {
   int32_t world, rank;            /* 1 <= world <= 8 */
   int32_t num_rows, num_heads, head_dim; /* head_dim % 4 == 0; H % world == 0 for scatter */
   int32_t mode;                   /* QMLA_DCP_ALL_HEADS or QMLA_DCP_HEAD_SCATTER */
-  uint32_t epoch;                 /* this step's epoch (>= 1), equal on every rank */
+  uint32_t epoch;                 /* this step's epoch (>= 1, equal on every rank); 0 = device epoch */
   void* out;                      /* [B, heads of this rank, D] */
   int64_t out_stride_row, out_stride_head; /* elements */
   int32_t out_dtype;              /* QMLA_DT_BF16 / F16 / F32 */

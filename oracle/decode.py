@@ -35,7 +35,8 @@ def _rms_values(rows: np.ndarray, heads: int, rms_offset: int, mode: str, kv_fp8
 def decode(q: np.ndarray, cache: np.ndarray, block_table: np.ndarray, seq_lens: np.ndarray, *,
            rank: int, qk_dim: int, page_size: int, sm_scale: float, rms_offset: int = -1,
            rms_mode: str = "native", kv_fp8: bool = False, k_scale: float = 1.0,
-           logit_cap: float = 0.0, dequant_to_bf16: bool = True) -> tuple[np.ndarray, np.ndarray]:
+           logit_cap: float = 0.0, dequant_to_bf16: bool = True,
+           chunk: int = 65536) -> tuple[np.ndarray, np.ndarray]:
     """Paged latent decode: returns (o [rows, H, rank], lse [rows, H]) in float64.
 
     Follows the Triton kernel's order (qwen_mla/ops/mla_decode_attention.py:440-586 for one
@@ -49,37 +50,49 @@ def decode(q: np.ndarray, cache: np.ndarray, block_table: np.ndarray, seq_lens: 
     test reference does (tests/test_fp8_kv.py:56-58, 61-72).
     rms_mode: "none" | "native" | "bf16" | "log8".  Rows with length <= 0 give o = 0 and
     lse = -inf (the reference divides 0 by 0 there; this build defines them as empty).
+    Rows longer than ``chunk`` tokens are processed ``chunk`` tokens at a time with a running
+    max, sum and weighted sum in float64 (the split-K merge of :1064-1137 with equal splits), so a
+    262,144-token row needs a few hundred MB, not gigabytes.
     """
     rows_n, H = q.shape[0], q.shape[1]
     o = np.zeros((rows_n, H, rank), dtype=np.float64)
     lse = np.full((rows_n, H), -np.inf, dtype=np.float64)
     ks = np.float32(k_scale)
+    bt_all = np.asarray(block_table)
     for r in range(rows_n):
         L = int(seq_lens[r])
         if L <= 0:
             continue
-        t = np.arange(L)
-        pages = np.asarray(block_table[r])[t // page_size].astype(np.int64)
-        rows = cache[pages, t % page_size]  # [L, W]
-        if kv_fp8:
-            K = e4m3_decode(rows[:, :qk_dim]) * ks
-            if dequant_to_bf16:
-                K = bf16_round(K)
-        else:
-            K = bf16_bits_to_f32(rows[:, :qk_dim])
-        K = K.astype(np.float64)
-        s = q[r, :, :qk_dim].astype(np.float64) @ K.T  # [H, L]
-        if rms_offset >= 0 and rms_mode != "none":
-            rms = _rms_values(rows, H, rms_offset, rms_mode, kv_fp8, float(ks)).astype(np.float64)
-            s = s / np.where(rms > 0, rms, 1.0).T
-        s = s * float(np.float32(sm_scale))
-        if logit_cap > 0:
-            s = logit_cap * np.tanh(s / logit_cap)
-        m = s.max(axis=1, keepdims=True)
-        p = np.exp(s - m)
-        den = p.sum(axis=1, keepdims=True)
-        o[r] = (p @ K[:, :rank]) / den
-        lse[r] = (m + np.log(den))[:, 0]
+        qr = q[r, :, :qk_dim].astype(np.float64)
+        m_run = np.full((H, 1), -np.inf)
+        den = np.zeros((H, 1))
+        acc = np.zeros((H, rank))
+        for t0 in range(0, L, max(1, int(chunk))):
+            t = np.arange(t0, min(L, t0 + int(chunk)))
+            pages = bt_all[r][t // page_size].astype(np.int64)
+            rows = cache[pages, t % page_size]  # [n, W]
+            if kv_fp8:
+                K = e4m3_decode(rows[:, :qk_dim]) * ks
+                if dequant_to_bf16:
+                    K = bf16_round(K)
+            else:
+                K = bf16_bits_to_f32(rows[:, :qk_dim])
+            K = K.astype(np.float64)
+            s = qr @ K.T  # [H, n]
+            if rms_offset >= 0 and rms_mode != "none":
+                rms = _rms_values(rows, H, rms_offset, rms_mode, kv_fp8, float(ks)).astype(np.float64)
+                s = s / np.where(rms > 0, rms, 1.0).T
+            s = s * float(np.float32(sm_scale))
+            if logit_cap > 0:
+                s = logit_cap * np.tanh(s / logit_cap)
+            m_new = np.maximum(m_run, s.max(axis=1, keepdims=True))
+            alpha = np.exp(m_run - m_new)  # 0 on the first chunk (m_run = -inf)
+            p = np.exp(s - m_new)
+            den = den * alpha + p.sum(axis=1, keepdims=True)
+            acc = acc * alpha + p @ K[:, :rank]
+            m_run = m_new
+        o[r] = acc / den
+        lse[r] = (m_run + np.log(den))[:, 0]
     return o, lse
 
 

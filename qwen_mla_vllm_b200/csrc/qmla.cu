@@ -701,7 +701,7 @@ int qmla_dcp_buffer_free(void* ptr) {
 int qmla_dcp_p2p_merge(const qmla_dcp_p2p_params* p, void* stream) {
   if (!p || p->world < 1 || p->world > kDcpMaxWorld || p->rank < 0 || p->rank >= p->world ||
       p->num_rows < 0 || p->num_heads <= 0 || p->head_dim <= 0 || p->head_dim % 4 != 0 ||
-      !p->out || p->epoch == 0 || p->out_dtype < 0 || p->out_dtype > 2 ||
+      !p->out || p->out_dtype < 0 || p->out_dtype > 2 ||
       (p->mode != QMLA_DCP_ALL_HEADS && p->mode != QMLA_DCP_HEAD_SCATTER))
     return QMLA_E_INVALID;
   if (p->mode == QMLA_DCP_HEAD_SCATTER && p->num_heads % p->world != 0) return QMLA_E_INVALID;

@@ -25,7 +25,11 @@
 namespace qmla {
 
 constexpr int kDcpMaxWorld = 8;
-constexpr int kDcpHeader = 256;  // flags[kDcpMaxWorld] (u32), status (u32), padding
+constexpr int kDcpHeader = 256;  // flags[kDcpMaxWorld] (u32), status (u32), padding, stats
+constexpr int kDcpStatusOffset = 32;  // u32 status word (QMLA_DEV_ERR_* bits)
+constexpr int kDcpEpochOffset = 36;   // u32 last epoch this rank merged (device-epoch mode)
+constexpr int kDcpDoneOffset = 40;    // u32 blocks of the running merge that have finished
+constexpr int kDcpStatsOffset = 64;   // u64 [launches, flag-wait ns, total ns] of block 0
 
 // Byte offsets inside one rank's exchange buffer.
 struct ExchangeLayout {
@@ -43,7 +47,7 @@ struct ExchangeLayout {
 struct P2PArgs {
   uint8_t* bufs[kDcpMaxWorld];  // every rank's exchange buffer, mapped on this device
   int world, rank, B, H, D, mode;
-  uint32_t epoch;
+  uint32_t epoch;  // 0: device-epoch mode (the epoch is the header's last epoch + 1)
   uint8_t* out;
   int64_t out_sr, out_sh;
   int out_dtype;
@@ -68,33 +72,45 @@ __global__ void __launch_bounds__(128) dcp_p2p_merge_kernel(const P2PArgs a) {
   const int tid = threadIdx.x;
   const ExchangeLayout L = ExchangeLayout::make(a.B, a.H, a.D);
   uint32_t* my_flags = reinterpret_cast<uint32_t*>(a.bufs[a.rank]);
+  // Block 0 stamps its entry, the end of its flag wait and its exit (%globaltimer) and adds the
+  // wait and the total to the stats of this rank's own header: the host reads how long a step
+  // waited for the slowest peer apart from the merge itself.
+  const bool stamp = blockIdx.x == 0 && tid == 0;
+  const uint64_t t_enter = stamp ? globaltimer_ns() : 0ull;
+  // The step's epoch: the host's, or (epoch 0) one past the last epoch this rank merged, kept in
+  // its own header so a replayed CUDA graph advances it.  The previous merge on this stream set
+  // that word after all of its blocks had finished, so every block reads the same value.
+  uint32_t* my_epoch = reinterpret_cast<uint32_t*>(a.bufs[a.rank] + kDcpEpochOffset);
+  const uint32_t epoch = a.epoch != 0u ? a.epoch : *reinterpret_cast<volatile uint32_t*>(my_epoch) + 1u;
   // 1. publish: this rank's partial (written by the preceding decode on this stream) is complete
   if (tid < a.world && tid != a.rank) {
     __threadfence_system();
-    st_release_sys_u32(reinterpret_cast<uint32_t*>(a.bufs[tid]) + a.rank, a.epoch);
+    st_release_sys_u32(reinterpret_cast<uint32_t*>(a.bufs[tid]) + a.rank, epoch);
   }
   // 2. wait (bounded) for every peer's flag in this rank's own buffer
   if (tid == 0) fail_s = 0;
   __syncthreads();
   if (tid < a.world && tid != a.rank) {
     const uint64_t t0 = globaltimer_ns();
-    while ((int)(ld_acquire_sys_u32(my_flags + tid) - a.epoch) < 0) {
+    while ((int)(ld_acquire_sys_u32(my_flags + tid) - epoch) < 0) {
       if (globaltimer_ns() - t0 > (uint64_t)a.timeout_ns) {
         fail_s = 1;
-        atomicOr(reinterpret_cast<int*>(my_flags + kDcpMaxWorld), QMLA_DEV_ERR_TIMEOUT);
+        atomicOr(reinterpret_cast<int*>(a.bufs[a.rank] + kDcpStatusOffset), QMLA_DEV_ERR_TIMEOUT);
         break;
       }
       __nanosleep(64);
     }
   }
   __syncthreads();
-  if (fail_s) return;
-  // 3. merge
+  const uint64_t t_waited = stamp ? globaltimer_ns() : 0ull;
+  // 3. merge (skipped after a wait that gave up; the epoch bookkeeping below still runs, so the
+  // next step does not reuse this one's epoch)
   const int hs = a.mode == 1 ? a.H / a.world : a.H;
   const int h0 = a.mode == 1 ? a.rank * hs : 0;
-  const int slot = (int)(a.epoch & 1u);
+  const int slot = (int)(epoch & 1u);
+  const int n_items = fail_s ? 0 : a.B * hs;
   const int osz = dt_size(a.out_dtype);
-  for (int item = blockIdx.x; item < a.B * hs; item += gridDim.x) {
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
     const int b = item / hs, hl = item - b * hs, h = h0 + hl;
     if (tid < 32) {
       float v = -INFINITY;
@@ -135,6 +151,22 @@ __global__ void __launch_bounds__(128) dcp_p2p_merge_kernel(const P2PArgs a) {
     }
     if (tid == 0 && a.lse_out) a.lse_out[(int64_t)b * hs + hl] = lse_s;
     __syncthreads();  // w_s / lse_s are rewritten by the next item
+  }
+  // device-epoch mode: the last block to finish records this epoch as merged
+  if (a.epoch == 0u && tid == 0) {
+    unsigned int* done = reinterpret_cast<unsigned int*>(a.bufs[a.rank] + kDcpDoneOffset);
+    __threadfence();
+    if (atomicAdd(done, 1u) == gridDim.x - 1) {
+      *done = 0u;
+      *reinterpret_cast<volatile uint32_t*>(my_epoch) = epoch;
+      __threadfence();
+    }
+  }
+  if (stamp) {
+    unsigned long long* st = reinterpret_cast<unsigned long long*>(a.bufs[a.rank] + kDcpStatsOffset);
+    atomicAdd(st + 0, 1ull);
+    atomicAdd(st + 1, (unsigned long long)(t_waited - t_enter));
+    atomicAdd(st + 2, (unsigned long long)(globaltimer_ns() - t_enter));
   }
 }
 

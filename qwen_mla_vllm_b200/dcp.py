@@ -97,6 +97,26 @@ def shard_lengths(seq_lens: list[int], world: int, rank: int) -> list[int]:
     return [hi - lo for lo, hi in (shard_bounds(int(L), world, rank) for L in seq_lens)]
 
 
+def head_group_of(rank: int, world: int, groups: int) -> tuple[int, int, int]:
+    """GLA head-group sharding: (head group, rank inside the group's split-KV sub-group, sub-group
+    size) of ``rank``.  The ``groups`` latent head groups (each with its own cache, rank-local
+    latent ``r / groups``: ``qwen_mla/mla_impl.py:182-200``) are spread over the ranks in order:
+    group g on ranks [g * world/groups, (g+1) * world/groups).  With world == groups each GPU
+    holds one group and nothing is exchanged; with more ranks each group is additionally split by
+    KV over its sub-group and merged there (the same LSE merge as DCP)."""
+    if world % groups:
+        raise ValueError(f"{world} ranks do not split into {groups} head groups")
+    per = world // groups
+    return rank // per, rank % per, per
+
+
+def head_group_subgroups(world: int, groups: int) -> list:
+    """One process group per head group (ranks of head_group_of).  Every rank must call this, in
+    the same order, before using any of them (torch.distributed.new_group's rule)."""
+    per = world // groups
+    return [dist.new_group(list(range(g * per, (g + 1) * per))) for g in range(groups)]
+
+
 def lse_all_gather(lse: torch.Tensor, group=None) -> torch.Tensor:
     """[B,H] fp32 per rank -> [N,B,H] on every rank."""
     world = dist.get_world_size(group)
@@ -145,7 +165,7 @@ class _DeviceArray:
 
 
 def _device_view(ptr: int, shape: tuple, device, dtype=torch.float32) -> torch.Tensor:
-    typestr = {torch.float32: "<f4", torch.int32: "<i4"}[dtype]
+    typestr = {torch.float32: "<f4", torch.int32: "<i4", torch.int64: "<i8"}[dtype]
     return torch.as_tensor(_DeviceArray(ptr, shape, typestr), device=device)
 
 
@@ -167,8 +187,9 @@ class ExchangeBuffer:
         self.ptr = ptr.value
 
     def flags(self) -> torch.Tensor:
-        """The header: flags[8] (epoch published by each rank) and the status word."""
-        return _device_view(self.ptr, (_lib.DCP_MAX_WORLD + 1,), self.device, torch.int32)
+        """The header: flags[8] (epoch published by each rank), the status word, the last merged
+        epoch (device-epoch mode) and the merge's block counter."""
+        return _device_view(self.ptr, (_lib.DCP_MAX_WORLD + 3,), self.device, torch.int32)
 
     def partial(self, epoch: int) -> tuple[torch.Tensor, torch.Tensor]:
         """(o [B,H,D] f32, lse [B,H] f32) views of slot epoch & 1."""
@@ -176,6 +197,11 @@ class ExchangeBuffer:
         o = _device_view(self.ptr + self.o_off + slot * self.o_slot, (self.B, self.H, self.D), self.device)
         lse = _device_view(self.ptr + self.lse_off + slot * self.lse_slot, (self.B, self.H), self.device)
         return o, lse
+
+    def merge_stats(self) -> torch.Tensor:
+        """The header's merge statistics (int64 view): merges, ns waiting for the peers' flags, ns
+        from entry to exit, summed over the merges of this rank since the last ``zero_()``."""
+        return _device_view(self.ptr + 64, (3,), self.device, torch.int64)
 
     def status(self) -> int:
         st = ctypes.c_int32()
@@ -193,7 +219,8 @@ class ExchangeBuffer:
 def p2p_merge(bufs: list[int], rank: int, B: int, H: int, D: int, epoch: int, out: torch.Tensor,
               mode: str = "rs", lse_out: torch.Tensor | None = None, timeout_s: float = 2.0) -> None:
     """Launch ``qmla_dcp_p2p_merge`` for this rank over the exchange buffers ``bufs``
-    (device addresses on this device, one per rank, this rank's own included)."""
+    (device addresses on this device, one per rank, this rank's own included).  ``epoch`` 0
+    takes the step's epoch from the device (the rank's last merged epoch + 1)."""
     world = len(bufs)
     if not 1 <= world <= _lib.DCP_MAX_WORLD:
         raise ValueError(f"world {world} outside 1..{_lib.DCP_MAX_WORLD}")
@@ -228,7 +255,7 @@ class P2PExchange:
     """
 
     def __init__(self, num_rows: int, num_heads: int, head_dim: int, group=None, device=None,
-                 timeout_s: float = 2.0):
+                 timeout_s: float = 2.0, device_epoch: bool = True):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -238,6 +265,10 @@ class P2PExchange:
                                    else torch.device(device).index)
         self.B, self.H, self.D = num_rows, num_heads, head_dim
         self.timeout_s = timeout_s
+        # device_epoch: the merge kernel keeps the step's epoch in device memory (epoch 0 at the
+        # C ABI), so steps captured in a CUDA graph can be replayed; self.epoch mirrors it on the
+        # host for slot selection (a captured sequence must hold an even number of merges).
+        self.device_epoch = device_epoch
         self.buf = ExchangeBuffer(num_rows, num_heads, head_dim, self.device)
         handles = [None] * self.world
         dist.all_gather_object(handles, bytes(self.buf.handle.raw), group=group)
@@ -265,8 +296,8 @@ class P2PExchange:
         hs = self.H // self.world if mode == "rs" else self.H
         if out is None:
             out = torch.empty(self.B, hs, self.D, dtype=out_dtype, device=self.device)
-        p2p_merge(self.ptrs, self.rank, self.B, self.H, self.D, self.epoch, out, mode, lse_out,
-                  self.timeout_s)
+        p2p_merge(self.ptrs, self.rank, self.B, self.H, self.D, 0 if self.device_epoch else self.epoch, out,
+                  mode, lse_out, self.timeout_s)
         return out, lse_out
 
     def status(self) -> int:

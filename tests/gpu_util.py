@@ -95,3 +95,23 @@ def compare(o, lse, ref_o, ref_lse, *, tol, lse_tol=2e-2, rel_tol=None):
             le = float(np.abs(l[fin] - ref_lse[fin]).max())
             assert le < lse_tol, f"lse err {le:.3e}"
     return err, rel
+
+
+def oracle_rows(w, case, rows, chunk=65536):
+    """oracle.decode on the given decode rows of a bench workload case (only their pages are
+    copied to the host).  Returns (o [len(rows), H, rank], lse [len(rows), H]) in float64."""
+    page = w.page
+    bt_rows = case.bt_rows.cpu()
+    sl = case.sl_rows.cpu().numpy()
+    need = sorted({int(p) for r in rows for p in bt_rows[r, :(int(sl[r]) + page - 1) // page].tolist()})
+    remap = {p: i for i, p in enumerate(need)}
+    idx = torch.tensor(need, device=case.cache.device)
+    host = cache_numpy(case.cache[idx])
+    bt = np.zeros((len(rows), bt_rows.shape[1]), np.int32)
+    for i, r in enumerate(rows):
+        npg = (int(sl[r]) + page - 1) // page
+        bt[i, :npg] = [remap[int(p)] for p in bt_rows[r, :npg].tolist()]
+    q = case.q[rows].float().cpu().numpy()
+    return oracle.decode(q, host, bt, sl[rows], rank=w.rank, qk_dim=w.qk, page_size=page, sm_scale=1 / 16,
+                         rms_offset=w.qk, rms_mode="log8" if w.fp8 else "native", kv_fp8=w.fp8,
+                         k_scale=float(case.k_scale) if case.k_scale is not None else 1.0, chunk=chunk)

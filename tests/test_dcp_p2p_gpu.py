@@ -82,3 +82,52 @@ def test_p2p_merge_wait_times_out(cuda_device):
     finally:
         for b in bufs:
             b.free()
+
+
+def test_p2p_merge_device_epoch_and_graph_replay(cuda_device):
+    """Device-epoch mode (epoch 0 at the C ABI): each merge takes the rank's last merged epoch
+    + 1 from its header, reads slot epoch & 1 and advances the header, so a CUDA graph of two
+    merges replays correctly.  The peers' flags are set far ahead, so no wait blocks."""
+    from qwen_mla_vllm_b200.dcp import p2p_merge
+    B, H, D, world = 3, 8, 256, 2
+    rng = np.random.default_rng(11)
+    parts = rng.standard_normal((2, world, B, H, D)).astype(np.float32)  # [slot, rank, ...]
+    lses = rng.standard_normal((2, world, B, H)).astype(np.float32)
+    bufs = _bufs(world, B, H, D, cuda_device)
+    try:
+        for n, b in enumerate(bufs):
+            for slot in (0, 1):
+                o, lse = b.partial(slot)
+                o.copy_(torch.from_numpy(parts[slot, n]))
+                lse.copy_(torch.from_numpy(lses[slot, n]))
+            b.flags()[:world] = 1000
+        want = [oracle.dcp_merge(parts[slot], lses[slot])[0] for slot in (0, 1)]
+        out = torch.empty(B, H, D, dtype=torch.float32, device=cuda_device)
+        for step in range(1, 4):  # epochs 1, 2, 3 -> slots 1, 0, 1
+            p2p_merge([b.ptr for b in bufs], 0, B, H, D, 0, out, "ar", timeout_s=1.0)
+            torch.cuda.synchronize()
+            assert int(bufs[0].flags()[9].item()) == step      # last merged epoch
+            assert int(bufs[0].flags()[10].item()) == 0        # block counter reset
+            assert np.allclose(out.cpu().numpy(), want[step & 1], rtol=1e-5, atol=1e-5)
+        outs = [torch.empty_like(out) for _ in range(2)]
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for k in range(2):
+                    p2p_merge([b.ptr for b in bufs], 0, B, H, D, 0, outs[k], "ar", timeout_s=1.0)
+        torch.cuda.current_stream().wait_stream(s)
+        for rep in range(3):  # each replay merges epochs 4+2rep (slot 0) and 5+2rep (slot 1)
+            outs[0].zero_()
+            outs[1].zero_()
+            g.replay()
+            torch.cuda.synchronize()
+            assert int(bufs[0].flags()[9].item()) == 5 + 2 * rep
+            assert np.allclose(outs[0].cpu().numpy(), want[0], rtol=1e-5, atol=1e-5)
+            assert np.allclose(outs[1].cpu().numpy(), want[1], rtol=1e-5, atol=1e-5)
+        assert bufs[0].status() == 0
+        del g
+    finally:
+        for b in bufs:
+            b.free()

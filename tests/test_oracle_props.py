@@ -171,3 +171,55 @@ def test_cache_write_then_gather_round_trip(mode):
     r = kpe[tok, rope:]
     want_rms = oracle.log8_decode(oracle.log8_encode(r)) if mode == "log8" else r
     assert np.array_equal(got[:, rank + rope:], want_rms)
+
+
+def _small_paged(fp8: bool, seed: int = 3):
+    rng = np.random.default_rng(seed)
+    H, rank, rope, page = 24, 256, 232, 16
+    lens = np.array([0, 1, 300, 777], dtype=np.int32)
+    pps = 49
+    P = len(lens) * pps
+    bt = rng.permutation(P).reshape(len(lens), pps).astype(np.int32)
+    q = oracle.bf16_round((rng.standard_normal((len(lens), H, rank + rope)) / 32).astype(np.float32))
+    if fp8:
+        lat = oracle.bf16_round(rng.standard_normal((P * page, rank)).astype(np.float32))
+        kpe = oracle.bf16_round(np.concatenate([rng.standard_normal((P * page, rope)),
+                                                rng.uniform(0.5, 2.0, (P * page, H))], 1).astype(np.float32))
+        rows = oracle.fp8_cache_rows(lat, kpe, 0.0125, rope, H, "log8")
+        cache = rows.reshape(P, page, -1)
+    else:
+        c = rng.standard_normal((P, page, rank + rope + H)).astype(np.float32)
+        c[..., rank + rope:] = rng.uniform(0.5, 2.0, (P, page, H))
+        cache = oracle.f32_to_bf16_bits(c)
+    return q, cache, bt, lens, dict(rank=rank, qk_dim=rank + rope, page_size=page, sm_scale=1 / 16,
+                                    rms_offset=rank + rope)
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_chunked_oracle_equals_whole_row(fp8):
+    """Streaming a row in chunks (the oracle's long-row mode) gives the whole-row result."""
+    q, cache, bt, lens, kw = _small_paged(fp8)
+    extra = dict(rms_mode="log8", kv_fp8=True, k_scale=0.0125) if fp8 else {}
+    o1, l1 = oracle.decode(q, cache, bt, lens, **kw, **extra)
+    o2, l2 = oracle.decode(q, cache, bt, lens, **kw, **extra, chunk=64)
+    np.testing.assert_allclose(o2, o1, rtol=1e-12, atol=1e-14)
+    np.testing.assert_allclose(l2[np.isfinite(l1)], l1[np.isfinite(l1)], rtol=1e-12)
+    assert np.array_equal(np.isfinite(l1), np.isfinite(l2))
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_torch_cpu_reference_matches_oracle(fp8):
+    """The torch CPU path timed as the reference arm computes what the oracle computes."""
+    from oracle.torch_ref import decode_paged
+    q, cache, bt, lens, kw = _small_paged(fp8)
+    extra = dict(rms_mode="log8", kv_fp8=True, k_scale=0.0125) if fp8 else {}
+    o1, l1 = oracle.decode(q, cache, bt, lens, **kw, **extra)
+    tc = torch.from_numpy(cache) if fp8 else torch.from_numpy(cache.view(np.int16)).view(torch.bfloat16)
+    o2, l2 = decode_paged(torch.from_numpy(q), tc, torch.from_numpy(bt), lens.tolist(), rank=kw["rank"],
+                          qk_dim=kw["qk_dim"], page_size=kw["page_size"], sm_scale=kw["sm_scale"],
+                          rms_offset=kw["rms_offset"], rms_mode="log8" if fp8 else "native",
+                          k_scale=0.0125 if fp8 else 1.0)
+    np.testing.assert_allclose(o2.numpy(), o1, atol=2e-5)
+    fin = np.isfinite(l1)
+    np.testing.assert_allclose(l2.numpy()[fin], l1[fin], atol=2e-5)
+    assert np.array_equal(np.isfinite(l2.numpy()), fin)
