@@ -33,7 +33,9 @@ def test_sharded_decode_merges_to_the_full_decode(cuda_device, fp8, world, inter
         run_params(bench.params_for(w, sh, parts[r], lses[r]), cuda_device)
     o, lse = merge_partials(parts, lses)
     torch.cuda.synchronize()
-    tol = 5e-3 if fp8 else 2e-3  # two decodes of the same data in different splits
+    # two decodes of the same data split differently: bf16 P is rounded per weight (2^-9), and rows of
+    # a few tokens have |o| ~ 1, so bf16 differs by a few 1e-3; FP8's hi + lo P is finer
+    tol = 5e-3 if fp8 else 1e-2
     assert float((o - o_ref).abs().max()) < tol
     fin = l_ref.isfinite()
     assert torch.equal(lse.isfinite(), fin)
