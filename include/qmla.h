@@ -96,7 +96,7 @@ typedef struct qmla_decode_params {
   const int32_t* seq_lens;
 
   int32_t num_rows;   /* decode rows (already flattened for MTP verify)      */
-  int32_t num_heads;  /* query heads per row (<= 32)                          */
+  int32_t num_heads;  /* query heads per row (<= 48)                          */
   int32_t rank;       /* latent width = value width (multiple of 128)        */
   int32_t qk_dim;     /* attention width: latent + rope (reference Lk)        */
   int32_t rms_offset; /* element (byte for FP8 rows) offset of the rms tail  */
@@ -104,7 +104,12 @@ typedef struct qmla_decode_params {
   float sm_scale;
   float logit_cap;      /* <= 0: off                                          */
   const float* k_scale; /* device fp32 scalar, FP8 dequant scale; NULL = 1.0  */
-  int32_t qrows;        /* MTP verify tokens per request (rows already flattened) */
+  int32_t qrows;        /* MTP verify tokens per request (rows already flattened:
+                         * the qrows consecutive rows of a request share its block-table
+                         * row; row j's length is that draft's causal length).  When
+                         * qrows > 1 divides num_rows, up to 48 / num_heads of a request's
+                         * rows are decoded together, so its cache is read once per such
+                         * group instead of once per row; results are the same.           */
 
   /* Outputs: o[row*o_stride_row + head*o_stride_head + d], d < rank;
    * lse[row*lse_stride_row + head] natural-log LSE of the scaled scores
@@ -121,7 +126,8 @@ typedef struct qmla_decode_params {
   int64_t workspace_bytes;
 
   /* Optional precomputed plan from qmla_plan (device copy of tile_prefix,
-   * num_rows + 1 entries).  NULL: the plan is built on the device. */
+   * num_rows + 1 entries).  NULL: the plan is built on the device.  Ignored when
+   * MTP rows are decoded together (qrows > 1), whose plan is per group. */
   const int32_t* plan_tile_prefix;
 
   int32_t num_ctas; /* persistent CTAs; 0 = one per SM */

@@ -158,6 +158,7 @@ class DeviceGuard {
 };
 
 struct Plan {
+  int fold, R, work_rows;  // decode rows folded into one work row, its query rows, work rows
   int npv, nb, nqk;
   int use_tma, run;
   int n_qk_slots, n_sub_qk, n_full_chunks, cps, v_groups;
@@ -172,11 +173,17 @@ struct Plan {
   uint32_t smem_total;
 };
 
-int make_plan(const qmla_decode_params* p, Plan* pl) {
+constexpr int kMaxQueryRows = 48;  // query rows of a work row the kernel is built for
+
+int make_plan_fold(const qmla_decode_params* p, Plan* pl, int fold) {
   if (!p || !p->q || !p->kv_cache || !p->block_table || !p->seq_lens || !p->o)
     return QMLA_E_INVALID;
   if (!p->q_pe && p->qk_dim > p->rank) return QMLA_E_INVALID;
-  if (p->num_rows < 0 || p->num_heads <= 0 || p->num_heads > 32) return QMLA_E_UNSUPPORTED;
+  if (p->num_rows < 0 || p->num_heads <= 0 || p->num_heads > kMaxQueryRows) return QMLA_E_UNSUPPORTED;
+  pl->fold = fold;
+  pl->R = fold * p->num_heads;
+  pl->work_rows = p->num_rows / fold;
+  if (pl->R > kMaxQueryRows) return QMLA_E_UNSUPPORTED;
   if (p->rank <= 0 || p->rank % 128 != 0) return QMLA_E_UNSUPPORTED;
   const int nb = p->rank / 128;
   if (!(nb == 2 || nb == 3 || nb == 4 || nb == 6)) return QMLA_E_UNSUPPORTED;
@@ -196,8 +203,8 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   if (p->kv_row_width < p->qk_dim || p->kv_stride_token < p->kv_row_width) return QMLA_E_INVALID;
 
   pl->nb = nb;
-  pl->nqk = p->num_heads <= 16 ? 16 : p->num_heads <= 24 ? 24 : 32;
-  pl->npv = pl->nqk <= 16 ? 16 : 32;
+  pl->nqk = pl->R <= 16 ? 16 : pl->R <= 24 ? 24 : pl->R <= 32 ? 32 : 48;
+  pl->npv = pl->nqk <= 16 ? 16 : pl->nqk <= 32 ? 32 : 48;
   // Pages holding whole runs of 16 tokens are loaded with TMA boxes (no shared
   // memory staging through L1); other page sizes with 16-byte cp.async gathers.
   pl->run = gcd_int(p->page_size, kTile);
@@ -232,7 +239,7 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   // FP8 (2.70 vs 2.63), so those keep it.
   pl->n_sub_qk = (pl->qk_bytes + 127) / 128;
   pl->n_full_chunks = pl->qk_bytes / 128;
-  bool paired = pl->use_tma && !fp8 && nb == 6;
+  bool paired = pl->use_tma && !fp8 && nb == 6 && pl->nqk <= 32;
   if (getenv("QMLA_NO_PAIR")) paired = false;  // test hook: the one-column layout
   pl->cps = paired ? 2 : 1;
   pl->v_groups = paired ? 3 : 1;
@@ -285,9 +292,9 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   if (nk * (int)kslot + nv * (int)vslot > budget) return QMLA_E_UNSUPPORTED;
   pl->nk = (uint32_t)nk;
   pl->nv = (uint32_t)nv;
-  // barriers, abort flag + TMEM slot, red[256] + hv[128] floats, tokptr[2][kTile]
+  // barriers, abort flag + TMEM slot, red[256] + hv[256] floats, tokptr[2][kTile]
   const uint32_t n_bars = 2 * (pl->nk + pl->nv) + 14 + kKdoneDepth + 4;
-  if ((n_bars * 8 + 15) / 16 * 16 + 16 + 1024 + 512 + 16 * kTile > misc_bytes)
+  if ((n_bars * 8 + 15) / 16 * 16 + 16 + 1024 + 1024 + 16 * kTile > misc_bytes)
     return QMLA_E_UNSUPPORTED;
   uint32_t off = 0;
   pl->off_kring = off;
@@ -311,13 +318,31 @@ int make_plan(const qmla_decode_params* p, Plan* pl) {
   pl->ws_bounds = w;
   w = align_up(w + 4 * ((int64_t)kMaxCtas + 1), 256);
   pl->ws_prefix = w;
-  w = align_up(w + 4 * ((int64_t)p->num_rows + 1), 256);
+  w = align_up(w + 4 * ((int64_t)pl->work_rows + 1), 256);
   pl->ws_plse = w;
-  w = align_up(w + 4 * (int64_t)2 * G * p->num_heads, 256);
+  w = align_up(w + 4 * (int64_t)2 * G * pl->R, 256);
   pl->ws_po = w;
-  w = align_up(w + 4 * (int64_t)2 * G * p->num_heads * p->rank, 256);
+  w = align_up(w + 4 * (int64_t)2 * G * pl->R * p->rank, 256);
   pl->ws_total = w;
   return QMLA_OK;
+}
+
+// MTP verify (qrows > 1, rows flattened per request): fold the largest divisor F of qrows with
+// F * heads <= 48 drafts into one work row, so the request's cache is read qrows / F times
+// instead of qrows times.  Falls back to one decode row per work row where the folded shape does
+// not fit (shared memory), or when allow_fold is false (test hook QMLA_NO_FOLD: never fold).
+int make_plan(const qmla_decode_params* p, Plan* pl, bool allow_fold = true) {
+  int fold = 1;
+  if (p && allow_fold && p->qrows > 1 && p->num_rows % p->qrows == 0 && !getenv("QMLA_NO_FOLD")) {
+    for (int f = p->qrows; f >= 2; --f)
+      if (p->qrows % f == 0 && f * p->num_heads <= kMaxQueryRows) {
+        fold = f;
+        break;
+      }
+  }
+  int rc = make_plan_fold(p, pl, fold);
+  if (rc == QMLA_E_UNSUPPORTED && fold > 1) rc = make_plan_fold(p, pl, 1);
+  return rc;
 }
 
 template <bool FP8, int NB, int NQK, bool PAIR>
@@ -326,10 +351,20 @@ int launch_decode_t(const CacheMaps& maps, const DecodeArgs& a, uint32_t smem,
   auto k = mla_decode_kernel<FP8, NB, NQK, PAIR>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
+  static bool regs_ok = true;
   std::call_once(once, [&] {
     attr_err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+    if constexpr (NQK >= 32) {
+      // the warpgroups' setmaxnreg budgets add up to exactly the pool of a CTA launched with
+      // kRegsAtLaunch registers per thread; with fewer, a setmaxnreg.inc would wait forever, so
+      // such a build is never launched
+      cudaFuncAttributes fa;
+      regs_ok = attr_err == cudaSuccess && cudaFuncGetAttributes(&fa, k) == cudaSuccess &&
+                fa.numRegs * kNumThreads >= (int)(kRegsSoftmax + kRegsProducer) * 256;
+    }
   });
   if (attr_err != cudaSuccess) return QMLA_E_CUDA;
+  if (!regs_ok) return QMLA_E_UNSUPPORTED;
   k<<<a.G, kNumThreads, smem, st>>>(maps, a);
   return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
 }
@@ -344,6 +379,9 @@ int launch_decode_nb(int nqk, const CacheMaps& maps, const DecodeArgs& a, uint32
       return launch_decode_t<FP8, NB, 24, PAIR>(maps, a, smem, st);
     case 32:
       return launch_decode_t<FP8, NB, 32, PAIR>(maps, a, smem, st);
+    case 48:
+      if constexpr (!PAIR) return launch_decode_t<FP8, NB, 48, false>(maps, a, smem, st);
+      break;
   }
   return QMLA_E_UNSUPPORTED;
 }
@@ -439,9 +477,14 @@ int qmla_decode_workspace_bytes(const qmla_decode_params* p, int64_t* bytes) {
   return QMLA_OK;
 }
 
-int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
+}  // extern "C"
+
+namespace {
+// qmla_mla_decode with the folding choice exposed (the static-scratch entry point turns folding
+// off when the folded partials would not fit its array).
+int decode_impl(const qmla_decode_params* p, void* stream, bool allow_fold) {
   Plan pl;
-  int rc = make_plan(p, &pl);
+  int rc = make_plan(p, &pl, allow_fold);
   if (rc != QMLA_OK) return rc;
   if (!p->workspace || p->workspace_bytes < pl.ws_total) return QMLA_E_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(p->workspace) % 256 != 0) return QMLA_E_ALIGNMENT;
@@ -474,7 +517,9 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
     a.token_stride_b = p->kv_stride_token * es;
     a.num_pages = p->kv_num_pages;
   }
-  a.num_rows = p->num_rows;
+  a.num_rows = pl.work_rows;
+  a.fold = pl.fold;
+  a.R = pl.R;
   a.H = p->num_heads;
   a.rank = p->rank;
   a.qk_dim = p->qk_dim;
@@ -503,8 +548,9 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
   a.lse_sr = p->lse_stride_row;
   a.lse_dtype = p->lse_dtype;
   a.status = reinterpret_cast<int*>(ws + pl.ws_status);
-  a.tile_prefix = p->plan_tile_prefix ? p->plan_tile_prefix
-                                      : reinterpret_cast<const int32_t*>(ws + pl.ws_prefix);
+  // a host plan (qmla_plan) is per decode row: used only when rows are not folded
+  const int32_t* host_prefix = pl.fold == 1 ? p->plan_tile_prefix : nullptr;
+  a.tile_prefix = host_prefix ? host_prefix : reinterpret_cast<const int32_t*>(ws + pl.ws_prefix);
   a.part_lse = reinterpret_cast<float*>(ws + pl.ws_plse);
   a.range_bounds = reinterpret_cast<const int32_t*>(ws + pl.ws_bounds);
   a.part_o = reinterpret_cast<float*>(ws + pl.ws_po);
@@ -534,28 +580,42 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
     if (rc != QMLA_OK) return rc;
   }
   int32_t* bounds = reinterpret_cast<int32_t*>(ws + pl.ws_bounds);
-  if (!p->plan_tile_prefix) {
-    plan_kernel<<<1, 1024, 0, st>>>(p->seq_lens, p->num_rows,
+  if (!host_prefix) {
+    plan_kernel<<<1, 1024, 0, st>>>(p->seq_lens, pl.work_rows, pl.fold,
                                     reinterpret_cast<int32_t*>(ws + pl.ws_prefix), a.status,
                                     a.G, a.seg_cost, bounds);
   } else {
-    bounds_kernel<<<1, 256, 0, st>>>(p->plan_tile_prefix, p->num_rows, a.status, a.G, a.seg_cost,
-                                     bounds);
+    bounds_kernel<<<1, 256, 0, st>>>(host_prefix, p->num_rows, a.status, a.G, a.seg_cost, bounds);
   }
   if (cudaGetLastError() != cudaSuccess) return QMLA_E_CUDA;
   rc = launch_decode(p->kv_dtype == QMLA_DT_FP8E4M3, pl.cps == 2, pl.nb, pl.nqk, maps, a,
                      pl.smem_total, st);
   if (rc != QMLA_OK) return rc;
-  split_merge_kernel<<<dim3(p->num_rows, p->num_heads), 128, 0, st>>>(a);
+  split_merge_kernel<<<dim3(pl.work_rows, pl.R), 128, 0, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
+}
+}  // namespace
+
+extern "C" {
+
+int qmla_mla_decode(const qmla_decode_params* p, void* stream) {
+  return decode_impl(p, stream, true);
 }
 
 int qmla_mla_decode_static(const qmla_decode_params* p, void* stream) {
   if (!p) return QMLA_E_INVALID;
-  int64_t need = 0;
-  int rc = qmla_decode_workspace_bytes(p, &need);
+  Plan pl;
+  int rc = make_plan(p, &pl, true);
   if (rc != QMLA_OK) return rc;
-  if (need > kStaticScratchBytes) return QMLA_E_WORKSPACE;
+  // MTP folding widens the per-CTA partials (fold x heads query rows); where that would not fit
+  // the array, decode the rows unfolded (same results, more cache reads)
+  bool allow_fold = true;
+  if (pl.ws_total > kStaticScratchBytes && pl.fold > 1) {
+    allow_fold = false;
+    rc = make_plan(p, &pl, false);
+    if (rc != QMLA_OK) return rc;
+  }
+  if (pl.ws_total > kStaticScratchBytes) return QMLA_E_WORKSPACE;
   DeviceGuard dg(p->device);
   if (!dg.ok()) return QMLA_E_CUDA;
   void* scratch = static_scratch(p->device);
@@ -566,7 +626,7 @@ int qmla_mla_decode_static(const qmla_decode_params* p, void* stream) {
   qmla_decode_params q = *p;
   q.workspace = scratch;
   q.workspace_bytes = kStaticScratchBytes;
-  return qmla_mla_decode(&q, stream);
+  return decode_impl(&q, stream, allow_fold);
 }
 
 int qmla_static_read_status(int32_t device, void* stream, int32_t* status) {

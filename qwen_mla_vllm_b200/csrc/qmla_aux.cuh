@@ -14,8 +14,9 @@ namespace qmla {
 // CTA range bounds of the decode kernel's partition (range_bound), and clears the device
 // status word.  One block of 1024 threads.  Partition rule shared with the host planner
 // (qmla_plan) for the prefix.
+// A work row is `fold` consecutive decode rows; its length is the longest of theirs.
 __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ seq_lens, int n,
-                                                    int32_t* __restrict__ prefix,
+                                                    int fold, int32_t* __restrict__ prefix,
                                                     int* __restrict__ status, int G, int seg_cost,
                                                     int32_t* __restrict__ bounds) {
   __shared__ int warp_sums[32];
@@ -31,7 +32,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
     int i = base + tid;
     int v = 0;
     if (i < n) {
-      int L = seq_lens[i];
+      int L = 0;
+      for (int d = 0; d < fold; ++d) L = max(L, seq_lens[(int64_t)i * fold + d]);
       v = L > 0 ? (L + kTile - 1) / kTile : 0;
     }
     int x = v;
@@ -75,20 +77,21 @@ __global__ void __launch_bounds__(256) bounds_kernel(const int32_t* __restrict__
 
 // Merge of the per-CTA partial segments of rows that crossed a CTA boundary
 // (the reference's stage 2, mla_decode_attention.py:1064-1137, over the
-// decode kernel's partition).  One block per (row, head); rows inside one CTA
-// range are final already.  Rows of length 0 get o = 0 and lse = -inf.
+// decode kernel's partition).  One block per (work row, query row); rows inside one CTA
+// range are final already.  Work rows of length 0 get o = 0 and lse = -inf.  Query row r
+// of work row g is head r % H of decode row g * fold + r / H.
 __global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
-  const int row = blockIdx.x, h = blockIdx.y;
+  const int row = blockIdx.x, r = blockIdx.y;
   const int plo = __ldg(a.tile_prefix + row), phi = __ldg(a.tile_prefix + row + 1);
   const int total = __ldg(a.tile_prefix + a.num_rows);
-  const int H = a.H, D = a.rank;
+  const int R = a.R, D = a.rank;
+  const int dq = r / a.H, h = r - dq * a.H;
   const int osz = dt_size(a.o_dtype);
-  uint8_t* orow = a.o + ((int64_t)row * a.o_sr + (int64_t)h * a.o_sh) * osz;
+  uint8_t* orow = a.o + (((int64_t)row * a.fold + dq) * a.o_sr + (int64_t)h * a.o_sh) * osz;
+  uint8_t* lrow = a.lse ? a.lse + (((int64_t)row * a.fold + dq) * a.lse_sr + h) * dt_size(a.lse_dtype) : nullptr;
   if (phi == plo) {
     for (int d = threadIdx.x; d < D; d += blockDim.x) store_from_float(orow + d * osz, a.o_dtype, 0.f);
-    if (a.lse && threadIdx.x == 0)
-      store_from_float(a.lse + ((int64_t)row * a.lse_sr + h) * dt_size(a.lse_dtype), a.lse_dtype,
-                       -INFINITY);
+    if (lrow && threadIdx.x == 0) store_from_float(lrow, a.lse_dtype, -INFINITY);
     return;
   }
   (void)total;
@@ -124,10 +127,10 @@ __global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
   __syncthreads();
   if (threadIdx.x == 0) {
     float m = -INFINITY;
-    for (int i = 0; i < np; ++i) m = fmaxf(m, a.part_lse[(int64_t)slots[i] * H + h]);
+    for (int i = 0; i < np; ++i) m = fmaxf(m, a.part_lse[(int64_t)slots[i] * R + r]);
     float sum = 0.f;
     for (int i = 0; i < np; ++i) {
-      const float w = (m == -INFINITY) ? 0.f : exp2f(a.part_lse[(int64_t)slots[i] * H + h] - m);
+      const float w = (m == -INFINITY) ? 0.f : exp2f(a.part_lse[(int64_t)slots[i] * R + r] - m);
       wts[i] = w;
       sum += w;
     }
@@ -138,11 +141,10 @@ __global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
   __syncthreads();
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float acc = 0.f;
-    for (int i = 0; i < np; ++i) acc += wts[i] * a.part_o[((int64_t)slots[i] * H + h) * D + d];
+    for (int i = 0; i < np; ++i) acc += wts[i] * a.part_o[((int64_t)slots[i] * R + r) * D + d];
     store_from_float(orow + d * osz, a.o_dtype, acc);
   }
-  if (a.lse && threadIdx.x == 0)
-    store_from_float(a.lse + ((int64_t)row * a.lse_sr + h) * dt_size(a.lse_dtype), a.lse_dtype, lse_g);
+  if (lrow && threadIdx.x == 0) store_from_float(lrow, a.lse_dtype, lse_g);
 }
 
 // DCP output correction for one rank (qwen_mla/dcp_fix.py:31-98): grid (B, H).

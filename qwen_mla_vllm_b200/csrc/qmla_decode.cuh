@@ -66,7 +66,13 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: P may reach 2^8 before
 constexpr int kBarSoftmax = 1;             // named barrier id of the softmax warps
 constexpr int kBarK = 2;                   // named barrier id of the K-load warps
 constexpr int kKdoneDepth = 8;
-constexpr int kEarlyQTiles = 16;           // segments this short stage the next Q early             // QK-done signals in flight (V loads trail QK)
+constexpr int kEarlyQTiles = 16;           // segments this short stage the next Q early
+// Register split of the widest shapes (32 or more query rows): the softmax warpgroups hold a
+// running max, sum and scale per query row (NQK / 2 of each per thread), more than the 128
+// registers a 512-thread CTA gives every thread; the loader / issuer warpgroups need far fewer.
+// (kRegsSoftmax + kRegsProducer) * 256 threads = 128 * 512: the whole launch pool, no more.
+constexpr uint32_t kRegsSoftmax = 184, kRegsProducer = 72;
+constexpr int kRegsAtLaunch = 128;
 // Tiles of a row bulk-prefetched into L2 ahead of the K loads (TMA mode).  Off: the
 // prefetches share the bulk-copy engine with the K boxes and evicted the latent lines
 // that the V loads re-read (DRAM bytes per launch rose from 1.07x to 1.47x of the
@@ -92,8 +98,12 @@ struct DecodeArgs {
   int page_size;
   int use_tma;   // 1: K tiles by TMA boxes of run_rows tokens (page_size % 16 == 0)
   int run_rows;  // tokens per TMA box: gcd(page_size, 128)
-  // geometry
-  int num_rows, H, rank, qk_dim, rms_mode;
+  // geometry.  A work row is `fold` consecutive decode rows (MTP drafts of one request, which
+  // share its block-table row) decoded together as R = fold * H query rows, so the request's
+  // cache is read once per work row instead of once per draft.
+  int num_rows;     // work rows (decode rows / fold)
+  int fold, R;      // decode rows per work row; query rows per work row (fold * H)
+  int H, rank, qk_dim, rms_mode;
   int qk_bytes;     // bytes of a cache row the QK contraction reads
   int row_bytes;    // bytes of a cache row (kv_row_width * element size)
   int n_qk_slots;   // K-ring slots loaded per tile (two 128-byte column chunks per slot)
@@ -118,8 +128,8 @@ struct DecodeArgs {
   int* status;
   const int32_t* tile_prefix;   // [num_rows + 1]
   const int32_t* range_bounds;  // [G + 1] first tile of each CTA range (range_bound)
-  float* part_o;               // [2*G][H][rank]
-  float* part_lse;             // [2*G][H] (log2 units)
+  float* part_o;               // [2*G][R][rank]
+  float* part_lse;             // [2*G][R] (log2 units)
   int G;
   // shared-memory layout (byte offsets from the 1024-aligned base)
   uint32_t off_kring, nk, off_vring, nv, off_q, q_chunk_bytes, off_p, p_bytes, off_rms, off_misc;
@@ -169,6 +179,18 @@ __device__ __forceinline__ uint8_t f32_to_e4m3(float x) {
 __device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
   __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)b, __NV_E4M3);
   return __half2float(__half(h));
+}
+
+// Tokens of work row g: the longest of its decode rows (lengths < 0 count as 0); each query
+// row masks the tokens past its own decode row's length.
+__device__ __forceinline__ int work_len(const int32_t* seq_lens, int fold, int g) {
+  int L = 0;
+  for (int d = 0; d < fold; ++d) L = max(L, __ldg(seq_lens + (int64_t)g * fold + d));
+  return L;
+}
+// Block-table row of work row g (its first decode row's: the drafts of a request share it).
+__device__ __forceinline__ const int32_t* work_bt(const DecodeArgs& a, int g) {
+  return a.block_table + (int64_t)g * a.fold * a.bt_stride;
 }
 
 // Segment iterator: the CTA's tile range [lo, hi) cut at row boundaries.
@@ -254,10 +276,13 @@ __device__ __forceinline__ void st_shared_u32(uint32_t a, uint32_t x) {
   asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(x) : "memory");
 }
 
-// Load N (4, 8, 12 or 16) consecutive 32-bit columns of this thread's TMEM lane.
+// Load N (4, 8, 12, 16 or 24) consecutive 32-bit columns of this thread's TMEM lane.
 template <int N>
 __device__ __forceinline__ void load_cols(uint32_t taddr, float* v) {
-  if constexpr (N == 16) {
+  if constexpr (N == 24) {
+    tmem_ld16(taddr, v);
+    tmem_ld8(taddr + 16, v + 16);
+  } else if constexpr (N == 16) {
     tmem_ld16(taddr, v);
   } else if constexpr (N == 12) {
     tmem_ld8(taddr, v);
@@ -325,8 +350,8 @@ __device__ __forceinline__ bool slot_plain(const DecodeArgs& a, int s) {
 template <bool FP8, int NB, int NQK, bool PAIR>
 __global__ void __launch_bounds__(kNumThreads, 1)
     mla_decode_kernel(const __grid_constant__ CacheMaps maps, const DecodeArgs a) {
-  static_assert(NQK % 8 == 0 && NQK >= 8 && NQK <= 32, "heads rounded to 8..32");
-  constexpr int NPV = NQK <= 16 ? 16 : 32;        // PV MMA N (multiple of 16)
+  static_assert(NQK % 8 == 0 && NQK >= 8 && NQK <= 48, "query rows rounded to 8..48");
+  constexpr int NPV = NQK <= 16 ? 16 : NQK <= 32 ? 32 : 48;  // PV MMA N (multiple of 16)
   // QK MMA N: heads rounded up to 16 for bf16 (the extra B rows are read from the next Q
   // chunk and only produce S columns nobody reads); the hi|lo q rows for FP8.
   constexpr int NQKM = FP8 ? 2 * NQK : NPV;
@@ -342,8 +367,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   constexpr int OW = NPV;                         // TMEM columns per O block
   constexpr int SWP = FP8 ? 2 * NPV : NPV;        // TMEM columns per S partial (hi|lo for FP8)
   constexpr int KP = 2;                           // S partials (one per QK issuer)
-  constexpr int SB = 2;                           // S buffers
   constexpr int SW = KP * SWP;                    // TMEM columns per S buffer
+  // S buffers: two (QK of tile k+1 overlaps the softmax of tile k) where TMEM holds them next to
+  // O; one for the widest shapes (48 FP8 query rows: O 6 x 48 + S 2 x 96 = 480 of 512 columns),
+  // where QK of the next tile waits until the softmax has loaded S into registers.
+  constexpr int SB = (NB * OW + 2 * SW <= 512) ? 2 : 1;
   constexpr uint32_t kCols = NB * OW + SB * SW;
   constexpr uint32_t kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128
                                  : kCols <= 256 ? 256 : 512;
@@ -401,9 +429,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc2);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc2 + 4);
   float* red = reinterpret_cast<float*>(misc2 + 16);  // [2 halves][4 sp][32]
-  float* hv = red + 256;                              // [4][32] per-head broadcast values
-  // hv[0..31] alpha, hv[32..63] l, hv[64..95] m, hv[96..127] q scale (FP8)
-  uint64_t* tokptr = reinterpret_cast<uint64_t*>(hv + 128);  // [2][128] K-load row addresses
+  float* hv = red + 256;                              // [4][64] per-query-row broadcast values
+  // hv[0..63] alpha, hv[64..127] l, hv[128..191] m, hv[192..255] q scale (FP8)
+  uint64_t* tokptr = reinterpret_cast<uint64_t*>(hv + 256);  // [2][128] K-load row addresses
 
   if (threadIdx.x == 0) {
     for (uint32_t i = 0; i < nk; ++i) {
@@ -436,6 +464,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  static_assert((kRegsSoftmax + kRegsProducer) * 256 <= kRegsAtLaunch * kNumThreads, "register pool");
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t col_o = 0;
   const uint32_t col_s = NB * OW;
@@ -448,6 +477,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const int rstride = 16 * a.rms_units;       // rms staging bytes per token
   int* status = a.status;
 
+  // Roles, one branch per warpgroup at the top so each warpgroup's register budget
+  // (setmaxnreg, same instruction for its four warps) governs all of its code.
+  if (warp >= kSoftmaxWarps) {
+  if constexpr (NQK >= 32) setmaxnreg_dec<kRegsProducer>();
   if (a.use_tma && warp == kWarpK) {
     // ====================================================== K loads by TMA
     // Per slot: one paired box per run of tokens within a page (both columns at once),
@@ -468,9 +501,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     Ring r;
     bool ok = true;
     while (ok && next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi)) {
-      int L = __ldg(a.seq_lens + row);
-      L = L < 0 ? 0 : L;
-      const int32_t* bt = a.block_table + (int64_t)row * a.bt_stride;
+      const int L = work_len(a.seq_lens, a.fold, row);
+      const int32_t* bt = work_bt(a, row);
       // page of token run `lane` of a tile (-1: past the row end, loads zeros)
       auto run_page = [&](int k) -> int {
         const int tok = k * kTile + lane * run;
@@ -536,9 +568,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     uint32_t jt = 0;
     bool ok = true;
     while (ok && next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi)) {
-      int L = __ldg(a.seq_lens + row);
-      L = L < 0 ? 0 : L;
-      const int32_t* bt = a.block_table + (int64_t)row * a.bt_stride;
+      const int L = work_len(a.seq_lens, a.fold, row);
+      const int32_t* bt = work_bt(a, row);
       for (int kp = k0; kp < min(k1, k0 + kPrefetchTiles); ++kp) {  // no-op unless enabled
         for (int h2 = 0; h2 < kTile / 32; ++h2) {
           const uint64_t pa = token_row_addr(a, bt, L, kp, lane + 32 * h2);
@@ -588,9 +619,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     Ring r;
     bool ok = true;
     while (ok && next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi)) {
-      int L = __ldg(a.seq_lens + row);
-      L = L < 0 ? 0 : L;
-      const int32_t* bt = a.block_table + (int64_t)row * a.bt_stride;
+      const int L = work_len(a.seq_lens, a.fold, row);
+      const int32_t* bt = work_bt(a, row);
       uint64_t nptr0 = token_row_addr(a, bt, L, k0, pt);
       uint64_t nptr1 = t1 >= 0 ? token_row_addr(a, bt, L, k0, t1) : 0ull;
       // optional L2 prefetch kPrefetchTiles ahead of the loads (off by default)
@@ -693,9 +723,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     Ring r;
     bool ok = active;
     while (ok && next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi)) {
-      int L = __ldg(a.seq_lens + row);
-      L = L < 0 ? 0 : L;
-      const int32_t* bt = a.block_table + (int64_t)row * a.bt_stride;
+      const int L = work_len(a.seq_lens, a.fold, row);
+      const int32_t* bt = work_bt(a, row);
       for (int k = k0; k < k1 && ok; ++k, ++jt) {
         // this lane's tokens of V slot half hh: hh*64 + gi*tpw + lane (and + 32 when one
         // warp covers the slot)
@@ -878,7 +907,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp < kSoftmaxWarps) {
+  }
+  } else {
+    if constexpr (NQK >= 32) setmaxnreg_inc<kRegsSoftmax>();
     // ====================================================== softmax / epilogue
     // Every wait result is folded into a barrier the whole group takes, so the
     // 256 threads always leave a tile (or the kernel) together.
@@ -887,31 +918,45 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const int hw = warp >> 2;     // head half
     const int tt = sp * 32 + lane;  // token of the tile (TMEM lane of S)
     const int H = a.H;
+    const int R = a.R;     // query rows of a work row: fold drafts x H heads
+    const int F = a.fold;
     constexpr int nqk = NQK;
     const uint32_t lane_base = (uint32_t)(sp * 32) << 16;
+    // This thread's query rows: head[j] = hw * NJ + j (draft head[j] / H, head head[j] % H).
     int head[NJ];
 #pragma unroll
     for (int j = 0; j < NJ; ++j) head[j] = hw * NJ + j;
+    // head (0..H-1) of query row hw * NJ + j: the rows of a thread are consecutive, so the head
+    // wraps at most NJ / H times (no division in the tile loop)
+    const int hq0 = (hw * NJ) % H;
+    auto head_in_row = [&](int j) -> int {
+      int h = hq0 + j;
+      while (h >= H) h -= H;
+      return h;
+    };
     // P^T / O^T column of head half hw, position j: hw * NH + j (j >= NJ is padding)
     auto head_of_n = [&](int n) -> int {
       const int j2 = n % NH;
       if (j2 >= NJ) return -1;
       const int h = (n / NH) * NJ + j2;
-      return h < H ? h : -1;
+      return h < R ? h : -1;
     };
     const float kscale = (FP8 && a.k_scale) ? __ldg(a.k_scale) : 1.0f;
     const bool cap = a.logit_cap > 0.f;
     const uint8_t* rms_smem = smem + a.off_rms;
     float m_ref[NJ], l_part[NJ], gs[NJ];
-    // Q of row qrow -> the Q buffer (bf16 rows, or e4m3 hi / lo rows with per-head scales in
-    // hv[96 + h] for FP8); all 256 softmax threads; arrives on qfull.
-    auto stage_q = [&](int qrow) {
+    // Q of work row wrow -> the Q buffer (bf16 rows, or e4m3 hi / lo rows with per-row scales in
+    // hv[192 + r] for FP8); query row r is head r % H of decode row wrow * F + r / H; all 256
+    // softmax threads; arrives on qfull.
+    auto stage_q = [&](int wrow) {
       if constexpr (!FP8) {
         const int upr = a.n_sub_qk * 8;  // 16-byte units (8 elements) per head row
         for (int i = tid; i < nqk * upr; i += kSoftmaxThreads) {
-          const int h = i / upr, u = i - h * upr, d0 = u * 8;
+          const int r = i / upr, u = i - r * upr, d0 = u * 8;
           uint32_t w[4] = {0u, 0u, 0u, 0u};
-          if (h < H && d0 < a.qk_dim) {
+          if (r < R && d0 < a.qk_dim) {
+            const int dq = r / H, h = r - dq * H;
+            const int64_t qrow = (int64_t)wrow * F + dq;
             const bool lat = d0 < a.rank;
             const uint8_t* src = lat ? a.q + ((int64_t)qrow * a.q_sr + (int64_t)h * a.q_sh + d0) * 2
                                      : a.q_pe + ((int64_t)qrow * a.qpe_sr + (int64_t)h * a.qpe_sh +
@@ -933,13 +978,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
               }
             }
           }
-          st_shared_v4(sw128(qbuf + (u >> 3) * a.q_chunk_bytes, h, u & 7), w[0], w[1], w[2], w[3]);
+          st_shared_v4(sw128(qbuf + (u >> 3) * a.q_chunk_bytes, r, u & 7), w[0], w[1], w[2], w[3]);
         }
       } else {
         // per-head scale so q*scale spans e4m3's range, then hi/lo split.  q elements
         // come 8 at a time (one 16-byte load when the row allows it; rank is a multiple of
         // 128, so a group of 8 never straddles the latent / rope boundary).
-        auto load8 = [&](int h, int d0, float* v) {
+        auto load8 = [&](int r, int d0, float* v) {
+          const int dq = r / H, h = r - dq * H;
+          const int64_t qrow = (int64_t)wrow * F + dq;
           const bool lat = d0 < a.rank;
           const uint8_t* src = lat ? a.q + ((int64_t)qrow * a.q_sr + (int64_t)h * a.q_sh + d0) * 2
                                    : a.q_pe + ((int64_t)qrow * a.qpe_sr + (int64_t)h * a.qpe_sh +
@@ -956,7 +1003,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
               v[e] = d0 + e < a.qk_dim ? load_as_float(src + 2 * e, a.q_dtype) : 0.f;
           }
         };
-        for (int h = warp; h < H; h += kSoftmaxWarps) {
+        for (int h = warp; h < R; h += kSoftmaxWarps) {  // h: query row
           float mx = 0.f;
           for (int d0 = lane * 8; d0 < a.qk_dim; d0 += 256) {
             float v[8];
@@ -966,7 +1013,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-          if (lane == 0) hv[96 + h] = mx > 0.f ? 448.f / mx : 1.f;
+          if (lane == 0) hv[192 + h] = mx > 0.f ? 448.f / mx : 1.f;
         }
         named_bar_sync(kBarSoftmax, kSoftmaxThreads);
         // one 16-element unit of one head per step: its hi bytes go to row h, lo to h + nqk
@@ -974,8 +1021,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         for (int i = tid; i < nqk * upr; i += kSoftmaxThreads) {
           const int h = i / upr, u = i - h * upr, d0 = u * 16;
           uint32_t whi[4] = {0u, 0u, 0u, 0u}, wlo[4] = {0u, 0u, 0u, 0u};
-          if (h < H && d0 < a.qk_dim) {
-            const float sc = hv[96 + h];
+          if (h < R && d0 < a.qk_dim) {
+            const float sc = hv[192 + h];
 #pragma unroll
             for (int half = 0; half < 2; ++half) {  // 8 elements at a time
               float v[8];
@@ -1015,15 +1062,22 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     bool have = next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi);
     if (have) stage_q(row);
     while (ok && have) {
-      int L = __ldg(a.seq_lens + row);
-      L = L < 0 ? 0 : L;
+      const int L = work_len(a.seq_lens, F, row);
+      // tokens query row head[j] sees: the length of its own decode row (MTP drafts are causal:
+      // draft d of a request sees L - (fold-1-d) tokens); 0 for padding rows
+      int lim[NJ];
 #pragma unroll
       for (int j = 0; j < NJ; ++j) {
         m_ref[j] = -INFINITY;
         l_part[j] = 0.f;
         float g = a.sm_scale;
-        if constexpr (FP8) g *= kscale / (head[j] < H ? hv[96 + head[j]] : 1.f);
+        if constexpr (FP8) g *= kscale / (head[j] < R ? hv[192 + head[j]] : 1.f);
         gs[j] = g;
+        lim[j] = 0;
+        if (head[j] < R) {
+          const int Ld = F == 1 ? L : __ldg(a.seq_lens + (int64_t)row * F + head[j] / H);
+          lim[j] = Ld < 0 ? 0 : Ld;
+        }
       }
 
       // ---------------- tiles
@@ -1041,19 +1095,19 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           tc_fence_after();
           const uint32_t tb = tmem_base + lane_base + col_s + sb * SW + hw * NJ;
           // S = sum of the KP partials (and of the hi / lo halves for FP8)
-          float xp[KP * (FP8 ? 2 : 1)][NJ];
+          // (one partial's columns in flight at a time: FP8's hi + lo of 24 rows are 48 registers)
 #pragma unroll
           for (int p = 0; p < KP; ++p) {
-            load_cols<NJ>(tb + p * SWP, xp[p * (FP8 ? 2 : 1)]);
-            if constexpr (FP8) load_cols<NJ>(tb + p * SWP + nqk, xp[p * 2 + 1]);
-          }
-          tmem_wait_ld();
+            float xp[FP8 ? 2 : 1][NJ];
+            load_cols<NJ>(tb + p * SWP, xp[0]);
+            if constexpr (FP8) load_cols<NJ>(tb + p * SWP + nqk, xp[1]);
+            tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < NJ; ++j) {
-            float v = 0.f;
-#pragma unroll
-            for (int p = 0; p < KP * (FP8 ? 2 : 1); ++p) v += xp[p][j];
-            x[j] = v;
+            for (int j = 0; j < NJ; ++j) {
+              float v = xp[0][j];
+              if constexpr (FP8) v += xp[1][j];
+              x[j] = p == 0 ? v : x[j] + v;
+            }
           }
           tc_fence_before();
           __syncwarp();
@@ -1070,8 +1124,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
               const uint8_t* rp = rms_smem + pb * (kTile * rstride) + tt * rstride + a.rms_skip;
 #pragma unroll
               for (int j = 0; j < NJ; ++j) {
-                if (head[j] < H) {
-                  const int h = head[j];
+                if (head[j] < R) {
+                  const int h = head_in_row(j);  // the divisor is per head, shared by the drafts
                   if (FP8 && a.rms_mode == 3) {
                     // 1 / rms = 2^(3 - code * 6/255)
                     f[j] = gs[j] * exp2f(3.0f - (float)rp[h] * (6.0f / 255.0f));
@@ -1106,7 +1160,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
         for (int j = 0; j < NJ; ++j) {
           float v = -INFINITY;
-          if (valid && head[j] < H) {
+          if (k * kTile + tt < lim[j]) {  // inside this query row's causal limit (0 for padding)
             float s = x[j] * f[j];
             if (cap) s = a.logit_cap * tanhf(s / a.logit_cap);
             v = s * kLog2e;
@@ -1150,7 +1204,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             // O holds tiles k0..k-1: wait for PV(k-1), then rescale it in TMEM
             if (sp == 0 && lane == 0) {
 #pragma unroll
-              for (int j = 0; j < NJ; ++j) hv[head[j] & 31] = alpha[j];
+              for (int j = 0; j < NJ; ++j) hv[head[j]] = alpha[j];
             }
             named_bar_sync(kBarSoftmax, kSoftmaxThreads);
             const uint32_t jp = jt - 1;
@@ -1224,14 +1278,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                 wlo[q4] |= (uint32_t)lo << (8 * e);
               }
             }
-            const uint32_t ah = prow + (n0 >> 4) * 128 + (n0 & 15);
-            const uint32_t al = prow + ((NPV + n0) >> 4) * 128 + ((NPV + n0) & 15);
             if constexpr (NH == 16) {
-              st_shared_v4(ah, whi[0], whi[1], whi[2], whi[3]);
-              st_shared_v4(al, wlo[0], wlo[1], wlo[2], wlo[3]);
+              st_shared_v4(prow + (n0 >> 4) * 128, whi[0], whi[1], whi[2], whi[3]);
+              st_shared_v4(prow + ((NPV + n0) >> 4) * 128, wlo[0], wlo[1], wlo[2], wlo[3]);
             } else {
-              st_shared_v2(ah, whi[0], whi[1]);
-              st_shared_v2(al, wlo[0], wlo[1]);
+              // 8 columns (8 bytes) at a time: column n sits in core matrix n / 16 at byte n % 16
+#pragma unroll
+              for (int g8 = 0; g8 < NH / 8; ++g8) {
+                const int n = n0 + 8 * g8, nl = NPV + n;
+                st_shared_v2(prow + (n >> 4) * 128 + (n & 15), whi[2 * g8], whi[2 * g8 + 1]);
+                st_shared_v2(prow + (nl >> 4) * 128 + (nl & 15), wlo[2 * g8], wlo[2 * g8 + 1]);
+              }
             }
           }
         }
@@ -1276,11 +1333,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         if (sp == 0 && lane == 0) {
 #pragma unroll
           for (int j = 0; j < NJ; ++j) {
-            if (head[j] < H) {
+            if (head[j] < R) {
               float lt = red[(hw * 4 + 0) * 32 + j] + red[(hw * 4 + 1) * 32 + j] +
                          red[(hw * 4 + 2) * 32 + j] + red[(hw * 4 + 3) * 32 + j];
-              hv[32 + head[j]] = lt;
-              hv[64 + head[j]] = m_ref[j];
+              hv[64 + head[j]] = lt;
+              hv[128 + head[j]] = m_ref[j];
             }
           }
         }
@@ -1293,41 +1350,49 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
         for (int i = 0; i < NPV / 2; ++i) {
           hn[i] = head_of_n(hw * (NPV / 2) + i);
-          float lt = hn[i] >= 0 ? hv[32 + hn[i]] : 0.f;
+          float lt = hn[i] >= 0 ? hv[64 + hn[i]] : 0.f;
           linv[i] = lt > 0.f ? oscale / lt : 0.f;
         }
         for (int blk = 0; blk < NB; ++blk) {
           const int d = blk * 128 + sp * 32 + lane;
           const uint32_t ta = tmem_base + lane_base + col_o + blk * OW + hw * (NPV / 2);
           float ov[NPV / 2];
-          if constexpr (NPV == 32)
+          if constexpr (NPV == 48) {
             tmem_ld16(ta, ov);
-          else
+            tmem_ld8(ta + 16, ov + 16);
+          } else if constexpr (NPV == 32) {
+            tmem_ld16(ta, ov);
+          } else {
             tmem_ld8(ta, ov);
+          }
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < NPV / 2; ++i) {
-            const int h = hn[i];
-            if (h >= 0) {
+            const int r = hn[i];  // query row: head r % H of decode row row * F + r / H
+            if (r >= 0) {
               const float v = ov[i] * linv[i];
-              if (full)
-                store_from_float(a.o + ((int64_t)row * a.o_sr + (int64_t)h * a.o_sh + d) *
+              if (full) {
+                const int dq = r / H;
+                store_from_float(a.o + (((int64_t)row * F + dq) * a.o_sr + (int64_t)(r - dq * H) * a.o_sh + d) *
                                            dt_size(a.o_dtype),
                                  a.o_dtype, v);
-              else
-                a.part_o[((int64_t)slot * H + h) * a.rank + d] = v;
+              } else {
+                a.part_o[((int64_t)slot * R + r) * a.rank + d] = v;
+              }
             }
           }
         }
-        if (tid < H) {
-          const float lt = hv[32 + tid];
-          const float l2 = hv[64 + tid] + log2f(lt);  // log2-domain LSE
+        if (tid < R) {
+          const float lt = hv[64 + tid];
+          const float l2 = hv[128 + tid] + log2f(lt);  // log2-domain LSE
           if (full) {
+            const int dq = tid / H;
             if (a.lse)
-              store_from_float(a.lse + ((int64_t)row * a.lse_sr + tid) * dt_size(a.lse_dtype),
+              store_from_float(a.lse + (((int64_t)row * F + dq) * a.lse_sr + (tid - dq * H)) *
+                                           dt_size(a.lse_dtype),
                                a.lse_dtype, l2 * kLn2);
           } else {
-            a.part_lse[(int64_t)slot * H + tid] = l2;
+            a.part_lse[(int64_t)slot * R + tid] = l2;
           }
         }
         tc_fence_before();

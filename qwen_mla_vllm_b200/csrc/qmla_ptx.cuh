@@ -187,6 +187,19 @@ __device__ __forceinline__ bool named_bar_or(int id, int nthreads, bool pred) {
   return out != 0;
 }
 
+// ---------------------------------------------------------------- register split
+// Per-warpgroup register budget (all four warps of a warpgroup execute the same one).  A .dec
+// hands registers back to the CTA's pool, an .inc waits until the pool has them: the sum over
+// the CTA's warpgroups must not exceed what the CTA was launched with, or the .inc never returns.
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),

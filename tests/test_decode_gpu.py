@@ -319,3 +319,59 @@ def test_entry_points_restore_current_device(cuda_device):
         torch.cuda.set_device(prev)
     ref_o, _ = oracle_ref(q, cache, bt, sl, rank=768, qk_dim=1000, page=16, sm_scale=1 / 16, rms_offset=1000)
     compare(o, None, ref_o, None, tol=BF16_TOL)
+
+
+@pytest.mark.parametrize("fp8,heads,qd,rank,rope", [(True, 24, 4, 768, 232), (False, 24, 2, 768, 232),
+                                                     (True, 12, 4, 384, 116), (False, 12, 3, 384, 116),
+                                                     (True, 24, 3, 768, 232), (False, 16, 3, 512, 128)])
+def test_mtp_rows_decoded_together(cuda_device, fp8, heads, qd, rank, rope, monkeypatch):
+    """MTP verify with a request's drafts decoded together (up to 48 query rows: 2 drafts x 24 heads,
+    4 x 12, 3 x 12, 3 x 16; 3 x 24 does not fold) against the oracle and, bit for bit where the
+    tiles are the same, against the row-by-row decode (QMLA_NO_FOLD).  Ragged requests include
+    drafts of length 0 (a request of length 2 with 4 drafts) and tile edges."""
+    lens_req = [1500, 2, 64, 900, 129, 1, 4097]
+    n = len(lens_req)
+    if fp8:
+        cache, _, bt_req, sl_req, ks = make_fp8_case(n, heads, rank, rope, 16, lens_req, seed=qd * 7 + heads,
+                                                     device=cuda_device)
+    else:
+        cache, _, bt_req, sl_req = make_bf16_case(n, heads, rank, rope, 16, lens_req, seed=qd * 7 + heads,
+                                                  device=cuda_device)
+        ks = None
+    bt_np, sl_np = oracle.mtp_flatten(bt_req.cpu().numpy(), sl_req.cpu().numpy(), qd)
+    bt = torch.from_numpy(bt_np).to(cuda_device)
+    sl = torch.from_numpy(sl_np).to(cuda_device)
+    g = torch.Generator().manual_seed(qd)
+    q = (torch.randn(n * qd, heads, rank + rope, generator=g) / 32).to(torch.bfloat16).to(cuda_device)
+    mode = "log8" if fp8 else "native"
+    o, lse = _run(q, cache, bt, sl, rank=rank, rms_offset=rank + rope, page=16, k_scale=ks, mode=mode, qrows=qd,
+                  o_dtype=torch.float32)
+    ref_o, ref_lse = oracle_ref(q, cache, bt, sl, rank=rank, qk_dim=rank + rope, page=16, sm_scale=1 / 16,
+                                rms_offset=rank + rope, rms_mode=mode, kv_fp8=fp8, k_scale=ks or 1.0)
+    compare(o, lse, ref_o, ref_lse, tol=FP8_TOL if fp8 else BF16_TOL, rel_tol=2e-2)
+    # drafts of length 0 are empty rows: o = 0, lse = -inf
+    zero = (sl == 0).nonzero().flatten().tolist()
+    assert zero and all(torch.all(o[r] == 0) and torch.all(lse[r] == -math.inf) for r in zero)
+    monkeypatch.setenv("QMLA_NO_FOLD", "1")
+    o1, lse1 = _run(q, cache, bt, sl, rank=rank, rms_offset=rank + rope, page=16, k_scale=ks, mode=mode, qrows=qd,
+                    o_dtype=torch.float32)
+    assert float((o1 - o).abs().max()) < (5e-3 if fp8 else 1e-2)
+    fin = torch.isfinite(lse1)
+    assert torch.equal(fin, torch.isfinite(lse)) and float((lse1[fin] - lse[fin]).abs().max()) < 1e-3
+    assert _status() == 0
+
+
+@pytest.mark.parametrize("heads,fp8", [(40, False), (48, True), (33, True)])
+def test_more_than_32_heads(cuda_device, heads, fp8):
+    """Up to 48 query heads per row (one decode row, no drafts)."""
+    lens = [700, 3, 2100]
+    if fp8:
+        cache, q, bt, sl, ks = make_fp8_case(len(lens), heads, 512, 128, 16, lens, seed=heads, device=cuda_device)
+    else:
+        cache, q, bt, sl = make_bf16_case(len(lens), heads, 512, 128, 16, lens, seed=heads, device=cuda_device)
+        ks = None
+    mode = "log8" if fp8 else "native"
+    o, lse = _run(q, cache, bt, sl, rank=512, rms_offset=640, page=16, k_scale=ks, mode=mode)
+    ref_o, ref_lse = oracle_ref(q, cache, bt, sl, rank=512, qk_dim=640, page=16, sm_scale=1 / 16, rms_offset=640,
+                                rms_mode=mode, kv_fp8=fp8, k_scale=ks or 1.0)
+    compare(o, lse, ref_o, ref_lse, tol=FP8_TOL if fp8 else BF16_TOL, rel_tol=2e-2)
