@@ -272,6 +272,16 @@ __device__ __forceinline__ void st_shared_v4(uint32_t a, uint32_t x, uint32_t y,
 __device__ __forceinline__ void st_shared_v2(uint32_t a, uint32_t x, uint32_t y) {
   asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(a), "r"(x), "r"(y) : "memory");
 }
+__device__ __forceinline__ uint32_t ld_shared_u32(uint32_t a) {
+  uint32_t x;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(x) : "r"(a));
+  return x;
+}
+__device__ __forceinline__ uint32_t ld_shared_u8(uint32_t a) {
+  uint32_t x;
+  asm volatile("ld.shared.u8 %0, [%1];" : "=r"(x) : "r"(a));
+  return x;
+}
 __device__ __forceinline__ void st_shared_u32(uint32_t a, uint32_t x) {
   asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(x) : "memory");
 }
@@ -366,12 +376,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   constexpr int kVTok = 64;                       // tokens per V slot (two per block and tile)
   constexpr int OW = NPV;                         // TMEM columns per O block
   constexpr int SWP = FP8 ? 2 * NPV : NPV;        // TMEM columns per S partial (hi|lo for FP8)
-  constexpr int KP = 2;                           // S partials (one per QK issuer)
+  // S partials: one per QK issuer (two issuers, each every other K step, when TMEM holds two
+  // double-buffered partials next to O); the widest FP8 shapes (48 query rows, hi | lo: 96
+  // columns per partial) keep one issuer and one partial so that S stays double-buffered (QK of
+  // tile k+1 overlaps the softmax of tile k): O 6 x 48 + S 2 x 96 = 480 of 512 columns.  A single
+  // S buffer with two partials measured 1.28x slower on config 2.
+  constexpr int KP = (NB * OW + 2 * 2 * SWP <= 512) ? 2 : 1;
   constexpr int SW = KP * SWP;                    // TMEM columns per S buffer
-  // S buffers: two (QK of tile k+1 overlaps the softmax of tile k) where TMEM holds them next to
-  // O; one for the widest shapes (48 FP8 query rows: O 6 x 48 + S 2 x 96 = 480 of 512 columns),
-  // where QK of the next tile waits until the softmax has loaded S into registers.
-  constexpr int SB = (NB * OW + 2 * SW <= 512) ? 2 : 1;
+  constexpr int SB = (NB * OW + 2 * SW <= 512) ? 2 : 1;  // S buffers
   constexpr uint32_t kCols = NB * OW + SB * SW;
   constexpr uint32_t kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128
                                  : kCols <= 256 ? 256 : 512;
@@ -773,11 +785,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (!ok) asm volatile("cp.async.wait_all;" ::: "memory");
   } else if (warp == kWarpQK || warp == kWarpQK + 1) {
     // ====================================================== QK issuers
-    // Each warp issues every other 16/32-wide K step of every column chunk into
-    // its own S partial (the softmax sums the partials): one thread issuing all
-    // MMAs of a tile was 10% slower overall.
+    // With two S partials each warp issues every other 16/32-wide K step of every column
+    // chunk into its own partial (the softmax sums them): one thread issuing all MMAs of a
+    // tile was 10% slower overall for 24 heads.  With one partial (KP = 1) warp 12 issues all.
     const int qw = warp - kWarpQK;
-    if (lane == 0) {
+    if (lane == 0 && qw < KP) {
       const uint32_t idesc = make_idesc_f16(FP8 ? 0 : 1, 128, NQKM, 0, 0);
       const uint32_t qc16 = a.q_chunk_bytes >> 4;              // Q chunk stride, descriptor units
       const uint64_t q_desc0 = make_sdesc(qbuf, 16, 1024, 2);  // Q chunk 0 (K-major, 128B swizzle)
@@ -817,8 +829,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                                            : make_sdesc(slot + ci * 1024, 16, 2048, 2);
                 const uint64_t bd0 = q_desc0 + (uint64_t)(c0 + ci) * qc16;
 #pragma unroll
-                for (int kk = 0; kk < 2; ++kk) {
-                  const int ks = 2 * kk + qw;
+                for (int kk = 0; kk < 4 / KP; ++kk) {  // 4 K steps of 32 bytes per column
+                  const int ks = KP * kk + qw;
                   const uint32_t acc = (s == 0 && ci == 0 && kk == 0) ? 0u : 1u;
                   if constexpr (FP8)
                     tc_mma_f8_ss(d_s, ad0 + (uint64_t)(ks * 2), bd0 + (uint64_t)(ks * 2), idesc, acc);
@@ -934,6 +946,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       while (h >= H) h -= H;
       return h;
     };
+    // the heads of this thread's query rows are consecutive (no wrap into the next draft)
+    const bool rms_contig = hq0 + min(NJ, R - hw * NJ) <= H;
     // P^T / O^T column of head half hw, position j: hw * NH + j (j >= NJ is padding)
     auto head_of_n = [&](int n) -> int {
       const int j2 = n % NH;
@@ -943,7 +957,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     };
     const float kscale = (FP8 && a.k_scale) ? __ldg(a.k_scale) : 1.0f;
     const bool cap = a.logit_cap > 0.f;
-    const uint8_t* rms_smem = smem + a.off_rms;
     float m_ref[NJ], l_part[NJ], gs[NJ];
     // Q of work row wrow -> the Q buffer (bf16 rows, or e4m3 hi / lo rows with per-row scales in
     // hv[192 + r] for FP8); query row r is head r % H of decode row wrow * F + r / H; all 256
@@ -1113,30 +1126,55 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(b_sempty + sb));
         }
+        if (tid == 0) QMLA_TR(14);
         // ---- rms divisor -> per-(token, head) factor
         float f[NJ];
 #pragma unroll
         for (int j = 0; j < NJ; ++j) f[j] = gs[j];
         if (a.rms_units > 0 && ok) {
           ok = mbar_wait(bar(b_rfull + pb), (jt >> 1) & 1, abort_flag, status);
+          if (tid == 0 && a.use_tma) QMLA_TR(1);  // (event 1 is the cp.async K loader's otherwise)
           if (ok) {
             if (valid) {
-              const uint8_t* rp = rms_smem + pb * (kTile * rstride) + tt * rstride + a.rms_skip;
+              // this token's staged rms tail (shared memory): one value per head, shared by a
+              // work row's drafts; es bytes per head (bf16 values / raw bf16 bytes, or one code)
+              const uint32_t rrow = rmsbuf + pb * (kTile * rstride) + tt * rstride + a.rms_skip;
+              const int es = (!FP8 || a.rms_mode == 2) ? 2 : 1;
+              auto factor = [&](int j, uint32_t bits) -> float {
+                if (FP8 && a.rms_mode == 3)  // 1 / rms = 2^(3 - code * 6/255)
+                  return gs[j] * exp2f(3.0f - (float)bits * (6.0f / 255.0f));
+                const float rv = (!FP8 || a.rms_mode == 2)
+                                     ? __bfloat162float(__ushort_as_bfloat16((uint16_t)bits))
+                                     : e4m3_to_f32((uint8_t)bits) * kscale;
+                return rv > 0.f ? __fdividef(gs[j], rv) : gs[j];
+              };
+              if (rms_contig) {
+                // heads hq0 .. hq0 + NJ - 1 lie side by side in the row: a few aligned 32-bit
+                // loads realigned by funnel shifts, instead of a byte load per head
+                constexpr int NW = NJ / 2 + 2;  // covers NJ two-byte heads plus the misalignment
+                const uint32_t addr = rrow + (uint32_t)(hq0 * es);
+                const uint32_t a4 = addr & ~3u, sh = (addr & 3u) * 8u;
+                const int nw = (int)(((addr & 3u) + (uint32_t)(NJ * es) + 3u) >> 2);
+                uint32_t w[NW];
 #pragma unroll
-              for (int j = 0; j < NJ; ++j) {
-                if (head[j] < R) {
-                  const int h = head_in_row(j);  // the divisor is per head, shared by the drafts
-                  if (FP8 && a.rms_mode == 3) {
-                    // 1 / rms = 2^(3 - code * 6/255)
-                    f[j] = gs[j] * exp2f(3.0f - (float)rp[h] * (6.0f / 255.0f));
-                  } else {
-                    float rv;
-                    if (!FP8 || a.rms_mode == 2)
-                      rv = __bfloat162float(__ushort_as_bfloat16(
-                          (uint16_t)rp[2 * h] | ((uint16_t)rp[2 * h + 1] << 8)));
-                    else
-                      rv = e4m3_to_f32(rp[h]) * kscale;
-                    f[j] = rv > 0.f ? __fdividef(gs[j], rv) : gs[j];
+                for (int k = 0; k < NW; ++k) w[k] = k < nw ? ld_shared_u32(a4 + 4 * k) : 0u;
+#pragma unroll
+                for (int k = 0; k + 1 < NW; ++k) w[k] = __funnelshift_r(w[k], w[k + 1], sh);
+                if (es == 1) {
+#pragma unroll
+                  for (int j = 0; j < NJ; ++j)
+                    if (head[j] < R) f[j] = factor(j, (w[j >> 2] >> ((j & 3) * 8)) & 0xffu);
+                } else {
+#pragma unroll
+                  for (int j = 0; j < NJ; ++j)
+                    if (head[j] < R) f[j] = factor(j, (w[j >> 1] >> ((j & 1) * 16)) & 0xffffu);
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < NJ; ++j) {
+                  if (head[j] < R) {
+                    const uint32_t b = rrow + (uint32_t)(head_in_row(j) * es);
+                    f[j] = factor(j, es == 1 ? ld_shared_u8(b) : ld_shared_u8(b) | (ld_shared_u8(b + 1) << 8));
                   }
                 }
               }
@@ -1145,6 +1183,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             if (lane == 0) mbar_arrive(bar(b_rempty + pb));
           }
         }
+        if (tid == 0) QMLA_TR(15);
         // PV(jt-2) must be done before P buffer pb is rewritten
         if (jt >= 2 && ok) {
           const uint32_t jp = jt - 2;

@@ -331,6 +331,7 @@ def test_mtp_rows_decoded_together(cuda_device, fp8, heads, qd, rank, rope, monk
     drafts of length 0 (a request of length 2 with 4 drafts) and tile edges."""
     lens_req = [1500, 2, 64, 900, 129, 1, 4097]
     n = len(lens_req)
+    monkeypatch.setenv("QMLA_FOLD_ALWAYS", "1")  # fold FP8 rank 768 x 24 heads too (not the default)
     if fp8:
         cache, _, bt_req, sl_req, ks = make_fp8_case(n, heads, rank, rope, 16, lens_req, seed=qd * 7 + heads,
                                                      device=cuda_device)
