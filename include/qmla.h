@@ -97,8 +97,8 @@ typedef struct qmla_decode_params {
 
   int32_t num_rows;   /* decode rows (already flattened for MTP verify)      */
   int32_t num_heads;  /* query heads per row (<= 48)                          */
-  int32_t rank;       /* latent width = value width (multiple of 128)        */
-  int32_t qk_dim;     /* attention width: latent + rope (reference Lk)        */
+  int32_t rank;       /* latent width = value width: 256, 384, 512, 768 or 1792 */
+  int32_t qk_dim;     /* attention width: latent + rope (reference Lk), <= 2048 */
   int32_t rms_offset; /* element (byte for FP8 rows) offset of the rms tail  */
   int32_t rms_mode;   /* QMLA_RMS_*                                           */
   float sm_scale;

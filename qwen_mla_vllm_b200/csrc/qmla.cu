@@ -186,8 +186,10 @@ int make_plan_fold(const qmla_decode_params* p, Plan* pl, int fold) {
   if (pl->R > kMaxQueryRows) return QMLA_E_UNSUPPORTED;
   if (p->rank <= 0 || p->rank % 128 != 0) return QMLA_E_UNSUPPORTED;
   const int nb = p->rank / 128;
-  if (!(nb == 2 || nb == 3 || nb == 4 || nb == 6)) return QMLA_E_UNSUPPORTED;
-  if (p->qk_dim < p->rank || p->qk_dim > 1024) return QMLA_E_UNSUPPORTED;
+  if (!(nb == 2 || nb == 3 || nb == 4 || nb == 6 || nb == 14)) return QMLA_E_UNSUPPORTED;
+  if (p->qk_dim < p->rank || p->qk_dim > 2048) return QMLA_E_UNSUPPORTED;
+  // rank 1792 (14 output blocks): O takes 14 x 32 TMEM columns, so at most 32 query rows
+  if (nb == 14 && fold * p->num_heads > 32) return QMLA_E_UNSUPPORTED;
   if (p->page_size <= 0) return QMLA_E_INVALID;
   if (p->q_dtype != QMLA_DT_BF16 && p->q_dtype != QMLA_DT_F16) return QMLA_E_UNSUPPORTED;
   if (p->o_dtype < 0 || p->o_dtype > 2) return QMLA_E_UNSUPPORTED;
@@ -366,8 +368,9 @@ int launch_decode_t(const CacheMaps& maps, const DecodeArgs& a, uint32_t smem,
       // kRegsAtLaunch registers per thread; with fewer, a setmaxnreg.inc would wait forever, so
       // such a build is never launched
       cudaFuncAttributes fa;
+      // (registers are allocated to a warp in units of 8 per thread)
       regs_ok = attr_err == cudaSuccess && cudaFuncGetAttributes(&fa, k) == cudaSuccess &&
-                fa.numRegs * kNumThreads >= (int)(kRegsSoftmax + kRegsProducer) * 256;
+                (fa.numRegs + 7) / 8 * 8 * kNumThreads >= (int)(kRegsSoftmax + kRegsProducer) * 256;
     }
   });
   if (attr_err != cudaSuccess) return QMLA_E_CUDA;
@@ -387,7 +390,7 @@ int launch_decode_nb(int nqk, const CacheMaps& maps, const DecodeArgs& a, uint32
     case 32:
       return launch_decode_t<FP8, NB, 32, PAIR>(maps, a, smem, st);
     case 48:
-      if constexpr (!PAIR) return launch_decode_t<FP8, NB, 48, false>(maps, a, smem, st);
+      if constexpr (!PAIR && NB * 48 <= 448) return launch_decode_t<FP8, NB, 48, false>(maps, a, smem, st);
       break;
   }
   return QMLA_E_UNSUPPORTED;
@@ -405,6 +408,8 @@ int launch_decode_fp(int nb, int nqk, const CacheMaps& maps, const DecodeArgs& a
       return launch_decode_nb<FP8, 4, false>(nqk, maps, a, smem, st);
     case 6:
       return launch_decode_nb<FP8, 6, false>(nqk, maps, a, smem, st);
+    case 14:
+      return launch_decode_nb<FP8, 14, false>(nqk, maps, a, smem, st);
   }
   return QMLA_E_UNSUPPORTED;
 }

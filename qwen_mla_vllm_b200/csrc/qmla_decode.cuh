@@ -51,7 +51,7 @@
 namespace qmla {
 
 constexpr int kTile = 128;         // tokens per tile (the QK MMA's M)
-constexpr int kMaxQkChunks = 16;   // QK width <= 1024 elements
+constexpr int kMaxQkChunks = 32;   // QK width <= 2048 bf16 elements (4 KB)
 constexpr int kMaxCtas = 160;      // persistent CTAs per launch (B200: 148 SMs)
 constexpr int kSoftmaxWarps = 8;
 constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;

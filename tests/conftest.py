@@ -24,7 +24,7 @@ def load_golden(name: str) -> dict:
 
 DECODE_FIXTURES = ["bf16_tp1_r768", "bf16_tp1_r256", "bf16_tp2_r384", "numerics_r256_h24",
                    "fp8_log8_r256", "fp8_bf16_r256", "fp8_e4m3_r256", "fp8_log8_r768",
-                   "fp8_log8_tp2_r384"]
+                   "fp8_log8_tp2_r384", "bf16_tp1_r1792", "bf16_tp2_r1792", "fp8_log8_r1792"]
 
 
 GATHER_FIXTURES = ["gather_auto", "gather_log8", "gather_log8_f16", "gather_bf16", "gather_e4m3"]

@@ -226,6 +226,11 @@ CASES = {
     "fp8_log8_r768": lambda t: fp8_case(t, batch=2, heads=24, ctx=100, rank=768, rope=232, mode="log8"),
     "fp8_log8_tp2_r384": lambda t: fp8_case(t, batch=2, heads=12, ctx=130, rank=384, rope=116, mode="log8"),
     "numerics_r256_h24": lambda t: numerics_case(t, rank=256, heads=24, ctx=100, batch=2),
+    # rank 1792, the reference's widest latent (tests/test_two_pass_1792.py: 24 heads | rope 232 and
+    # 12 heads | rope 116; tests/test_fp8_kv.py:137 covers FP8 at rank 1792)
+    "bf16_tp1_r1792": lambda t: partial_rope_case(t, batch=2, heads=24, ctx=90, rank=1792, rope=232),
+    "bf16_tp2_r1792": lambda t: partial_rope_case(t, batch=2, heads=12, ctx=90, rank=1792, rope=116),
+    "fp8_log8_r1792": lambda t: fp8_case(t, batch=2, heads=24, ctx=90, rank=1792, rope=232, mode="log8"),
     "cache_write_log8": lambda t: cache_write_case(t, "log8"),
     "cache_write_bf16": lambda t: cache_write_case(t, "bf16"),
     "rank_plan": lambda t: rank_plan_case(t),

@@ -251,11 +251,11 @@ def test_errors_are_raised(cuda_device):
     p.workspace, p.workspace_bytes = ws.data_ptr(), 256
     rc = _lib.load().qmla_mla_decode(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == -4
-    # rank 1792 (NB = 14) has no kernel in this build
-    big = torch.zeros(4, 16, 1, 2048, dtype=torch.bfloat16, device=cuda_device)
-    q2 = torch.zeros(1, 24, 2048, dtype=torch.bfloat16, device=cuda_device)
-    o2 = torch.zeros(1, 24, 1792, dtype=torch.bfloat16, device=cuda_device)
-    p2 = build_params(q2, big, o2, None, bt, sl, rank=1792, qk_dim=2024, rms_offset=2024, rms_mode=1,
+    # rank 640 (5 output blocks) has no kernel in this build
+    big = torch.zeros(4, 16, 1, 1024, dtype=torch.bfloat16, device=cuda_device)
+    q2 = torch.zeros(1, 24, 1024, dtype=torch.bfloat16, device=cuda_device)
+    o2 = torch.zeros(1, 24, 640, dtype=torch.bfloat16, device=cuda_device)
+    p2 = build_params(q2, big, o2, None, bt, sl, rank=640, qk_dim=872, rms_offset=872, rms_mode=1,
                       page_size=16, sm_scale=1 / 16)
     with pytest.raises(_lib.QmlaError) as e2:
         run_params(p2, cuda_device)
@@ -376,3 +376,29 @@ def test_more_than_32_heads(cuda_device, heads, fp8):
     ref_o, ref_lse = oracle_ref(q, cache, bt, sl, rank=512, qk_dim=640, page=16, sm_scale=1 / 16, rms_offset=640,
                                 rms_mode=mode, kv_fp8=fp8, k_scale=ks or 1.0)
     compare(o, lse, ref_o, ref_lse, tol=FP8_TOL if fp8 else BF16_TOL, rel_tol=2e-2)
+
+
+@pytest.mark.parametrize("heads,rope,page", [(24, 232, 784), (12, 116, 16), (24, 256, 16), (32, 232, 64)])
+def test_rank_1792(cuda_device, heads, rope, page):
+    """The reference's widest latent (rank 1792: 14 output blocks, QK width up to 2048), with the
+    shapes of its tests/test_two_pass_1792.py: 784-token pages, shuffled tables, ragged lengths, rms
+    spread; 12 and 24 heads with partial rope, 24 heads with full rope; 32 heads."""
+    lens = [4096, 1, 785, 2000, 0, 3333]
+    cache, q, bt, sl = make_bf16_case(len(lens), heads, 1792, rope, page, lens, seed=heads + rope, device=cuda_device,
+                                      rms_lo=0.2, rms_hi=4.0)
+    qk = 1792 + rope
+    o, lse = _run(q, cache, bt, sl, rank=1792, rms_offset=qk, page=page)
+    ref_o, ref_lse = oracle_ref(q, cache, bt, sl, rank=1792, qk_dim=qk, page=page, sm_scale=1 / 16, rms_offset=qk)
+    compare(o, lse, ref_o, ref_lse, tol=BF16_TOL, rel_tol=1e-2)
+    assert _status() == 0
+
+
+@pytest.mark.parametrize("page", [16, 784])
+def test_rank_1792_fp8(cuda_device, page):
+    """Rank 1792 on an FP8 cache with log8 rms codes (tests/test_fp8_kv.py:137 runs 1792 too)."""
+    lens = [3000, 17, 800]
+    cache, q, bt, sl, ks = make_fp8_case(len(lens), 24, 1792, 232, page, lens, seed=page, device=cuda_device)
+    o, lse = _run(q, cache, bt, sl, rank=1792, rms_offset=2024, page=page, k_scale=ks, mode="log8")
+    ref_o, ref_lse = oracle_ref(q, cache, bt, sl, rank=1792, qk_dim=2024, page=page, sm_scale=1 / 16,
+                                rms_offset=2024, rms_mode="log8", kv_fp8=True, k_scale=ks)
+    compare(o, lse, ref_o, ref_lse, tol=FP8_TOL, rel_tol=2e-2)
