@@ -12,6 +12,8 @@ Everything runs on the CPU.  The reference functions used (each called unmodifie
                                           its GPU cases at import time)
   * qwen_mla/mla_impl.py:309-342          QwenMLATritonImpl.do_kv_cache_update (FP8 row writer)
   * qwen_mla/fi_decode.py:235-270         _RankPlan.plan_cpu (work-list arrays)
+  * qwen_mla/mla_impl.py:628-662          MLATritonMetadataBuilder._build_decode (MTP rows, its
+                                          vLLM parent step stubbed)
   * qwen_mla/ops/mla_gather.py:28-76      gather_cache_torch (prefill context gather)
 Module-level constants the tests pin (PAGE, dev, SHUFFLE, ...) are set on the imported
 modules before the calls; shapes are kept small so the fixtures stay a few hundred KB each.
@@ -216,6 +218,35 @@ def rank_plan_case(tag, page=16):
     print(f"{tag}: {total} pages")
 
 
+def build_decode_case(tag, qd=4, width=70):
+    """MLATritonMetadataBuilder._build_decode (qwen_mla/mla_impl.py:628-662), run unmodified on a
+    stand-in builder: MTP verify rows flattened to one row per draft.  Its vLLM parent step
+    (super()._build_decode) is replaced for the call by a stub that returns the metadata object
+    holding the request-level block table and lengths, which the method then flattens."""
+    sys.path.insert(0, str(REF))
+    from qwen_mla.mla_impl import MLATritonMetadataBuilder as B
+    parent = next(c for c in B.__mro__[1:] if "_build_decode" in c.__dict__)
+    saved = parent.__dict__["_build_decode"]
+    parent._build_decode = lambda self, bt, sl, *a: types.SimpleNamespace(block_table=bt, seq_lens=sl)
+    try:
+        b = object.__new__(B)
+        b.vllm_config = types.SimpleNamespace(scheduler_config=types.SimpleNamespace(max_num_seqs=16))
+        b.reorder_batch_threshold = qd
+        g = torch.Generator().manual_seed(11)
+        n = 7
+        bt = torch.randint(0, 5000, (n, width), generator=g, dtype=torch.int32)
+        # lengths with drafts that clamp at 0 (CUDA-graph padding rows have length 0)
+        sl = torch.tensor([0, 1, 2, 3, 4, 129, 8192], dtype=torch.int32)
+        md = B._build_decode(b, bt, sl, int(sl.max()), None, None, n * qd, None)
+        q = int(getattr(md, "_mla_q"))
+        np.savez_compressed(HERE / f"{tag}.npz", block_table=bt.numpy(), seq_lens=sl.numpy(), qrows=q,
+                            flat_block_table=md.block_table.numpy(), flat_seq_lens=md.seq_lens.numpy(),
+                            source="qwen_mla/mla_impl.py:628-662")
+        print(f"{tag}: {n} requests x {q} drafts -> {md.block_table.shape[0]} rows")
+    finally:
+        parent._build_decode = saved
+
+
 CASES = {
     "bf16_tp1_r768": lambda t: partial_rope_case(t, batch=2, heads=24, ctx=100, rank=768, rope=232),
     "bf16_tp1_r256": lambda t: partial_rope_case(t, batch=2, heads=24, ctx=200, rank=256, rope=232),
@@ -234,6 +265,7 @@ CASES = {
     "cache_write_log8": lambda t: cache_write_case(t, "log8"),
     "cache_write_bf16": lambda t: cache_write_case(t, "bf16"),
     "rank_plan": lambda t: rank_plan_case(t),
+    "mtp_build_decode": lambda t: build_decode_case(t),
     "gather_auto": lambda t: gather_case(t, "auto"),
     "gather_log8": lambda t: gather_case(t, "log8"),
     "gather_log8_f16": lambda t: gather_case(t, "log8", dst_dtype=torch.float16),

@@ -68,3 +68,50 @@ def test_dcp_merge_matches_oracle(cuda_device, n):
     assert np.allclose(o.cpu().numpy(), want, rtol=1e-5, atol=1e-6)
     fin = np.isfinite(want_lse)
     assert np.allclose(lse.cpu().numpy()[fin], want_lse[fin], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("base_e", [True, False])
+def test_dcp_kernels_match_the_reference_correction(cuda_device, base_e):
+    """qmla_dcp_correct per rank, and the fused merges (qmla_dcp_merge, and the one-kernel P2P merge
+    with ranks emulated on one GPU) against the reference's own Triton correction
+    (qwen_mla/dcp_fix.py:101-130, fixture from tests/golden/make_golden_gpu.py): the merged
+    output is the sum of the ranks' corrected partials."""
+    from conftest import load_golden
+    from qwen_mla_vllm_b200.dcp import ExchangeBuffer, correct_attn_out, merge_partials, p2p_merge
+    g = load_golden("dcp_correct")
+    N, B, H, D = (int(g[k]) for k in ("N", "B", "H", "D"))
+    lses = torch.from_numpy(g["lses"]).to(cuda_device)
+    total = 0
+    for r in range(N):
+        key = f"{'e' if base_e else '2'}{r}"
+        o = torch.from_numpy(g["out"][r]).to(cuda_device).contiguous()
+        o, lse = correct_attn_out(o, lses, r, None, is_lse_base_on_e=base_e)
+        torch.cuda.synchronize()
+        assert torch.allclose(o.cpu(), torch.from_numpy(g[f"out_{key}"]), rtol=2e-6, atol=1e-6)
+        want = torch.from_numpy(g[f"lse_{key}"])
+        fin = torch.isfinite(want)
+        assert torch.equal(torch.isfinite(lse.cpu()), fin)
+        assert torch.allclose(lse.cpu()[fin], want[fin], rtol=1e-6, atol=1e-6)
+        total = total + g[f"out_{key}"]
+    if not base_e:
+        return  # the merges take natural-log LSEs
+    want = torch.from_numpy(total)
+    parts = torch.from_numpy(g["out"]).to(cuda_device).contiguous()
+    o, _ = merge_partials(parts, lses)
+    torch.cuda.synchronize()
+    assert torch.allclose(o.cpu(), want, rtol=1e-5, atol=1e-5)
+    bufs = [ExchangeBuffer(B, H, D, cuda_device) for _ in range(N)]
+    try:
+        for n, b in enumerate(bufs):
+            po, pl = b.partial(1)
+            po.copy_(parts[n])
+            pl.copy_(lses[n])
+            b.flags()[:N] = 1
+        out = torch.empty(B, H, D, dtype=torch.float32, device=cuda_device)
+        p2p_merge([b.ptr for b in bufs], 0, B, H, D, 1, out, "ar", timeout_s=1.0)
+        torch.cuda.synchronize()
+        assert bufs[0].status() == 0
+        assert torch.allclose(out.cpu(), want, rtol=1e-5, atol=1e-5)
+    finally:
+        for b in bufs:
+            b.free()

@@ -73,3 +73,43 @@ def test_gather_empty_and_fp8_without_layout():
                                fp8=True, mla_rms=(488, 24, "log8")).size == 0
     with pytest.raises(NotImplementedError):
         oracle.gather_cache(g["cache"], g["block_table"], g["cu_seq_lens"], g["token_to_seq"], 4, fp8=True)
+
+
+def test_mtp_flattening_matches_the_reference_builder():
+    """oracle.mtp_flatten and the product's plan_for_step flattening against the rows the
+    reference's own MLATritonMetadataBuilder._build_decode produced (qwen_mla/mla_impl.py:628-662),
+    bit for bit: block table per draft row, lengths L - (q-1-j) clamped at 0."""
+    import types
+
+    import torch
+
+    from qwen_mla_vllm_b200 import fi_decode
+    g = load_golden("mtp_build_decode")
+    q = int(g["qrows"])
+    bt, sl = oracle.mtp_flatten(g["block_table"], g["seq_lens"], q)
+    assert np.array_equal(bt, g["flat_block_table"])
+    assert np.array_equal(sl, g["flat_seq_lens"])
+    cfg = dict(device="cpu", rank=768, win=232, n_local=24, page_size=16, max_batch=64)
+    builder = types.SimpleNamespace(_mla_fi_cfg=cfg, _mla_fi_plan=None, _mla_fi_scale=1 / 16, _mla_fi_ok=True)
+    decode = types.SimpleNamespace(seq_lens=torch.from_numpy(g["flat_seq_lens"]),
+                                   block_table=torch.from_numpy(g["flat_block_table"]), _mla_q=q)
+    md = types.SimpleNamespace(decode=decode)
+    fi_decode.plan_for_step(builder, md, types.SimpleNamespace(_seq_lens_cpu=torch.from_numpy(g["seq_lens"])))
+    n = len(g["flat_seq_lens"])
+    assert np.array_equal(md._mla_fi_plan.kv_len[:n].numpy(), g["flat_seq_lens"])
+
+
+@pytest.mark.parametrize("base_e", [True, False])
+def test_dcp_correction_matches_the_reference_kernel(base_e):
+    """oracle.dcp_correct against the reference's own Triton DCP correction
+    (qwen_mla/dcp_fix.py:101-130, run on a GPU by tests/golden/make_golden_gpu.py): NaN / +inf
+    partial LSEs, rows empty on every rank or on some, every cp_rank, base e and base 2."""
+    g = load_golden("dcp_correct")
+    for r in range(int(g["N"])):
+        key = f"{'e' if base_e else '2'}{r}"
+        got, lse = oracle.dcp_correct(g["out"][r], g["lses"], r, is_base_e=base_e)
+        np.testing.assert_allclose(got, g[f"out_{key}"], rtol=2e-6, atol=1e-6)
+        want = g[f"lse_{key}"]
+        fin = np.isfinite(want)
+        assert np.array_equal(np.isfinite(lse), fin)
+        np.testing.assert_allclose(lse[fin], want[fin], rtol=1e-6, atol=1e-6)
