@@ -828,6 +828,7 @@ def dcp_line(w: Workload, d: Dist, steps: int, warmup: int, peaks: dict, group_w
     mine = w.algorithmic_bytes(shard.lens) // w.groups
     out = {"ms": ms, "decode_ms": dec_ms, "bytes": mine, "err": err, "lerr": lerr, "status": status,
            "wait_us": st[1] / max(st[0], 1) / 1e3, "merge_us": (st[2] - st[1]) / max(st[0], 1) / 1e3,
+           "publish_us": st[3] / max(st[0], 1) / 1e3,
            "ex": ex, "graphs": g_steps + g_dec, "shard": shard, "o_m": o_m, "lse_m": lse_m,
            "slot_params": slot_params, "o_ref": o_ref}
     return out
@@ -836,8 +837,8 @@ def dcp_line(w: Workload, d: Dist, steps: int, warmup: int, peaks: dict, group_w
 def summarize_dcp(name: str, w: Workload, d: Dist, r: dict, steps: int, peaks: dict, n_ranks: int,
                   groups_note: str) -> dict:
     """Reduce one DCP measurement over all ranks into a sub-object of the line."""
-    mx = d.reduce([r["ms"], r["decode_ms"], r["err"], r["lerr"], float(r["status"]), r["wait_us"], r["merge_us"]],
-                  "max")
+    mx = d.reduce([r["ms"], r["decode_ms"], r["err"], r["lerr"], float(r["status"]), r["wait_us"], r["merge_us"],
+                   r["publish_us"]], "max")
     mn = d.reduce([r["decode_ms"], r["wait_us"]], "min")
     tot = d.reduce([float(r["bytes"])], "sum")[0]
     ms = mx[0]
@@ -847,7 +848,7 @@ def summarize_dcp(name: str, w: Workload, d: Dist, r: dict, steps: int, peaks: d
             "hbm_frac_of_n_x_measured_peak": tbs * 1e3 / (peaks["hbm_gbs"] * n_ranks),
             "per_rank": {"decode_ms_min": mn[0], "decode_ms_max": mx[1],
                          "merge_flag_wait_us_min": mn[1], "merge_flag_wait_us_max": mx[5],
-                         "merge_kernel_us_max": mx[6],
+                         "merge_kernel_us_max": mx[6], "merge_publish_us_max": mx[7],
                          "note": "decode alone timed per rank over graph replays; the merge's flag wait "
                                  "and its merge time come from the kernel's %globaltimer stamps (block 0)"},
             "parity": {"max_abs": mx[2], "lse_max_abs": mx[3], "status": int(mx[4]),

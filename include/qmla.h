@@ -260,8 +260,9 @@ int qmla_gather_cache(const qmla_gather_params* p, void* stream);
  * Each rank of a DCP group (one process per GPU) owns one exchange buffer:
  *   [header 256 B: flags[8] u32 (epoch published by each rank), status u32 at byte 32,
  *    last merged epoch u32 at byte 36 and a block counter u32 at byte 40 (device-epoch mode),
- *    merge stats u64[3] at byte 64 (merges, ns spent waiting for the peers' flags, ns from
- *    entry to exit; block 0 of each qmla_dcp_p2p_merge adds to them; the host may zero them)]
+ *    merge stats u64[4] at byte 64 (merges, ns spent waiting for the peers' flags, ns from
+ *    entry to exit, ns to publish; block 0 of each qmla_dcp_p2p_merge adds to them; the host
+ *    may zero them)]
  *   [o partial, 2 slots of B*H*D f32, each 256-B aligned]
  *   [lse partial, 2 slots of B*H f32 (natural log), each 256-B aligned]
  * qmla_dcp_buffer_layout returns the byte offsets.  A decode step e writes the

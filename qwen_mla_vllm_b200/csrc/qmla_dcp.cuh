@@ -4,8 +4,8 @@
 // the other ranks have mapped through CUDA IPC.  A decode step writes the rank's
 // partial (o, lse) for its KV shard into slot (epoch & 1) of its own buffer; the
 // merge kernel then
-//   1. publishes "epoch ready" into each peer's flag word for this rank (every
-//      block stores it, so no block depends on another block being resident),
+//   1. publishes "epoch ready" into each peer's flag word for this rank (block 0 stores it; the
+//      grid is at most a few blocks per SM, so every block is resident at once),
 //   2. waits, bounded, until its own flag words show every peer at this epoch,
 //   3. reads the N partials of its (row, head) items straight from the peers'
 //      buffers and writes o = sum_n exp(lse_n - lse_g) o_n, lse_g = logsumexp lse_n
@@ -29,7 +29,7 @@ constexpr int kDcpHeader = 256;  // flags[kDcpMaxWorld] (u32), status (u32), pad
 constexpr int kDcpStatusOffset = 32;  // u32 status word (QMLA_DEV_ERR_* bits)
 constexpr int kDcpEpochOffset = 36;   // u32 last epoch this rank merged (device-epoch mode)
 constexpr int kDcpDoneOffset = 40;    // u32 blocks of the running merge that have finished
-constexpr int kDcpStatsOffset = 64;   // u64 [launches, flag-wait ns, total ns] of block 0
+constexpr int kDcpStatsOffset = 64;   // u64 [launches, flag-wait ns, total ns, publish ns] of block 0
 
 // Byte offsets inside one rank's exchange buffer.
 struct ExchangeLayout {
@@ -82,11 +82,14 @@ __global__ void __launch_bounds__(128) dcp_p2p_merge_kernel(const P2PArgs a) {
   // that word after all of its blocks had finished, so every block reads the same value.
   uint32_t* my_epoch = reinterpret_cast<uint32_t*>(a.bufs[a.rank] + kDcpEpochOffset);
   const uint32_t epoch = a.epoch != 0u ? a.epoch : *reinterpret_cast<volatile uint32_t*>(my_epoch) + 1u;
-  // 1. publish: this rank's partial (written by the preceding decode on this stream) is complete
-  if (tid < a.world && tid != a.rank) {
+  // 1. publish: this rank's partial (written by the preceding decode on this stream, complete at
+  // that kernel's end) is ready; one release store per peer, from block 0 only (a fence and a
+  // remote store from every block of the grid cost microseconds per step)
+  if (blockIdx.x == 0 && tid < a.world && tid != a.rank) {
     __threadfence_system();
     st_release_sys_u32(reinterpret_cast<uint32_t*>(a.bufs[tid]) + a.rank, epoch);
   }
+  const uint64_t t_pub = stamp ? globaltimer_ns() : 0ull;
   // 2. wait (bounded) for every peer's flag in this rank's own buffer
   if (tid == 0) fail_s = 0;
   __syncthreads();
@@ -167,6 +170,7 @@ __global__ void __launch_bounds__(128) dcp_p2p_merge_kernel(const P2PArgs a) {
     atomicAdd(st + 0, 1ull);
     atomicAdd(st + 1, (unsigned long long)(t_waited - t_enter));
     atomicAdd(st + 2, (unsigned long long)(globaltimer_ns() - t_enter));
+    atomicAdd(st + 3, (unsigned long long)(t_pub - t_enter));
   }
 }
 

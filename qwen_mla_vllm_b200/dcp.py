@@ -200,8 +200,9 @@ class ExchangeBuffer:
 
     def merge_stats(self) -> torch.Tensor:
         """The header's merge statistics (int64 view): merges, ns waiting for the peers' flags, ns
-        from entry to exit, summed over the merges of this rank since the last ``zero_()``."""
-        return _device_view(self.ptr + 64, (3,), self.device, torch.int64)
+        from entry to exit, ns to publish, summed over the merges of this rank since the last
+        ``zero_()``."""
+        return _device_view(self.ptr + 64, (4,), self.device, torch.int64)
 
     def status(self) -> int:
         st = ctypes.c_int32()
