@@ -342,6 +342,14 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(win)}
 
 
+def launches_per_call(work_rows: int) -> int:
+    """This build's kernels per qmla_mla_decode call: plan (or bounds) + decode, and the merge
+    kernel when there are fewer than a quarter as many work rows as persistent CTAs."""
+    import torch
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    return 2 + (1 if work_rows * 4 < sms else 0)
+
+
 def capture(fns, device):
     """One CUDA graph per callable (each called once eagerly before, so sizing is done)."""
     import torch
@@ -751,7 +759,7 @@ def single_gpu_line(w: Workload, device, steps: int, warmup: int, peaks: dict, g
            "algorithmic_bytes": nb, "seqs_per_s": len(w.lens) * len(list(groups)) / (ms * 1e-3),
            "roofline": {"bound": "hbm", "achieved": tbs * 1e3, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                         "frac": tbs * 1e3 / peaks["hbm_gbs"], "peak_source": peaks["kind"]},
-           "gpu_launches_per_step": 3 * len(params)}
+           "gpu_launches_per_step": launches_per_call(len(w.lens) * w.qrows) * len(params)}
     if w.qrows > 1:
         tf = fl / (ms * 1e-3) / 1e12
         res["tensor"] = {"algorithmic_flops": fl, "achieved_tflops": tf, "peak": peaks["bf16_tflops_sustained"],
@@ -906,7 +914,7 @@ def run_ours(args) -> None:
         t1 = time.perf_counter()
         total_bytes = float(w1.algorithmic_bytes())
         decode_ms = step_ms
-        launches = 3
+        launches = launches_per_call(len(w1.lens))
     else:
         pg = None
         r1 = dcp_line(w1, d, args.steps, args.warmup, peaks, world, rank, pg)
@@ -920,7 +928,7 @@ def run_ours(args) -> None:
         step_ms = s1["ms_per_step"]
         total_bytes = float(s1["algorithmic_bytes"])
         decode_ms = r1["decode_ms"]
-        launches = 4
+        launches = launches_per_call(len(w1.lens)) + 1  # + the P2P merge
         sub["dcp_cfg1"] = s1
     clocks = sampler.summary(t0, t1)
     value = total_bytes / (step_ms * 1e-3) / 1e12

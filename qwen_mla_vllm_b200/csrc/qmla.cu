@@ -167,7 +167,8 @@ struct Plan {
   int G;
   int q_vec, qpe_vec;
   // workspace offsets
-  int64_t ws_status, ws_bounds, ws_prefix, ws_plse, ws_po, ws_total;
+  int64_t ws_status, ws_bounds, ws_prefix, ws_done, ws_plse, ws_po, ws_total;
+  bool row_merge;  // rows cut at CTA boundaries are merged inside the decode kernel
   // smem
   uint32_t off_kring, nk, off_vring, nv, off_q, q_chunk, off_p, p_bytes, off_rms, off_misc;
   uint32_t smem_total;
@@ -321,6 +322,12 @@ int make_plan_fold(const qmla_decode_params* p, Plan* pl, int fold) {
   w = align_up(w + 4 * ((int64_t)kMaxCtas + 1), 256);
   pl->ws_prefix = w;
   w = align_up(w + 4 * ((int64_t)pl->work_rows + 1), 256);
+  // Many rows (each spans at most a few CTA ranges): the CTA that finishes a row's last piece
+  // merges it, and no merge kernel runs.  Few long rows (a row over many CTAs, as in DCP
+  // shards): the merge kernel spreads each row's merge over (row, query row) blocks instead.
+  pl->row_merge = (int64_t)pl->work_rows * 4 >= G && !getenv("QMLA_MERGE_KERNEL");
+  pl->ws_done = w;
+  w = align_up(w + 4 * (int64_t)pl->work_rows, 256);
   pl->ws_plse = w;
   w = align_up(w + 4 * (int64_t)2 * G * pl->R, 256);
   pl->ws_po = w;
@@ -566,6 +573,7 @@ int decode_impl(const qmla_decode_params* p, void* stream, bool allow_fold) {
   a.part_lse = reinterpret_cast<float*>(ws + pl.ws_plse);
   a.range_bounds = reinterpret_cast<const int32_t*>(ws + pl.ws_bounds);
   a.part_o = reinterpret_cast<float*>(ws + pl.ws_po);
+  a.row_done = pl.row_merge ? reinterpret_cast<int*>(ws + pl.ws_done) : nullptr;
   a.G = pl.G;
   a.off_kring = pl.off_kring;
   a.nk = pl.nk;
@@ -595,15 +603,16 @@ int decode_impl(const qmla_decode_params* p, void* stream, bool allow_fold) {
   if (!host_prefix) {
     plan_kernel<<<1, 1024, 0, st>>>(p->seq_lens, pl.work_rows, pl.fold,
                                     reinterpret_cast<int32_t*>(ws + pl.ws_prefix), a.status,
-                                    a.G, a.seg_cost, bounds);
+                                    a.G, a.seg_cost, bounds, a.row_done);
   } else {
-    bounds_kernel<<<1, 256, 0, st>>>(host_prefix, p->num_rows, a.status, a.G, a.seg_cost, bounds);
+    bounds_kernel<<<1, 256, 0, st>>>(host_prefix, p->num_rows, a.status, a.G, a.seg_cost, bounds,
+                                     a.row_done);
   }
   if (cudaGetLastError() != cudaSuccess) return QMLA_E_CUDA;
   rc = launch_decode(p->kv_dtype == QMLA_DT_FP8E4M3, pl.cps == 2, pl.nb, pl.nqk, maps, a,
                      pl.smem_total, st);
   if (rc != QMLA_OK) return rc;
-  split_merge_kernel<<<dim3(pl.work_rows, pl.R), 128, 0, st>>>(a);
+  if (!pl.row_merge) split_merge_kernel<<<dim3(pl.work_rows, pl.R), 128, 0, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
 }
 }  // namespace

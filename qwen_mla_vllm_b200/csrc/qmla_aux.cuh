@@ -18,7 +18,10 @@ namespace qmla {
 __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ seq_lens, int n,
                                                     int fold, int32_t* __restrict__ prefix,
                                                     int* __restrict__ status, int G, int seg_cost,
-                                                    int32_t* __restrict__ bounds) {
+                                                    int32_t* __restrict__ bounds,
+                                                    int* __restrict__ row_done) {
+  if (row_done)  // per-row piece counters of the decode kernel's in-kernel merge
+    for (int i = threadIdx.x; i < n; i += blockDim.x) row_done[i] = 0;
   __shared__ int warp_sums[32];
   __shared__ int carry_s;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -69,8 +72,11 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
 // device status word.  One block.
 __global__ void __launch_bounds__(256) bounds_kernel(const int32_t* __restrict__ prefix, int n,
                                                      int* __restrict__ status, int G, int seg_cost,
-                                                     int32_t* __restrict__ bounds) {
+                                                     int32_t* __restrict__ bounds,
+                                                     int* __restrict__ row_done) {
   if (threadIdx.x == 0 && status) *status = 0;
+  if (row_done)
+    for (int i = threadIdx.x; i < n; i += blockDim.x) row_done[i] = 0;
   for (int c = threadIdx.x; c <= G; c += blockDim.x)
     bounds[c] = range_bound(prefix, n, G, seg_cost, c);
 }

@@ -130,6 +130,7 @@ struct DecodeArgs {
   const int32_t* range_bounds;  // [G + 1] first tile of each CTA range (range_bound)
   float* part_o;               // [2*G][R][rank]
   float* part_lse;             // [2*G][R] (log2 units)
+  int* row_done;               // [num_rows] pieces written per work row (in-kernel merge), or null
   int G;
   // shared-memory layout (byte offsets from the 1024-aligned base)
   uint32_t off_kring, nk, off_vring, nv, off_q, q_chunk_bytes, off_p, p_bytes, off_rms, off_misc;
@@ -407,6 +408,25 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const int range_lo = __ldg(a.range_bounds + blockIdx.x);
   const int range_hi = __ldg(a.range_bounds + blockIdx.x + 1);
   (void)total;
+  if (a.row_done) {
+    // in-kernel merge mode (no merge kernel follows): work rows without tokens get o = 0 and
+    // lse = -inf here, row r by CTA r % G
+    for (int r = blockIdx.x; r < a.num_rows; r += gridDim.x) {
+      if (__ldg(a.tile_prefix + r + 1) != __ldg(a.tile_prefix + r)) continue;
+      const int osz = dt_size(a.o_dtype);
+      for (int i = threadIdx.x; i < a.R * a.rank; i += blockDim.x) {
+        const int q = i / a.rank, d = i - q * a.rank, dq = q / a.H;
+        store_from_float(a.o + (((int64_t)r * a.fold + dq) * a.o_sr + (int64_t)(q - dq * a.H) * a.o_sh + d) * osz,
+                         a.o_dtype, 0.f);
+      }
+      if (a.lse)
+        for (int q = threadIdx.x; q < a.R; q += blockDim.x) {
+          const int dq = q / a.H;
+          store_from_float(a.lse + (((int64_t)r * a.fold + dq) * a.lse_sr + (q - dq * a.H)) * dt_size(a.lse_dtype),
+                           a.lse_dtype, -INFINITY);
+        }
+    }
+  }
   if (range_lo >= range_hi) return;  // uniform for the whole CTA
   const int row0 = first_row_at(a.tile_prefix, a.num_rows, range_lo);
 #ifdef QMLA_TRACE
@@ -440,6 +460,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   uint8_t* misc2 = smem + a.off_misc + ((n_bars * 8 + 15) / 16) * 16;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc2);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc2 + 4);
+  volatile int* fix_flag = reinterpret_cast<volatile int*>(misc2 + 8);  // in-kernel merge: this CTA is last
   float* red = reinterpret_cast<float*>(misc2 + 16);  // [2 halves][4 sp][32]
   float* hv = red + 256;                              // [4][64] per-query-row broadcast values
   // hv[0..63] alpha, hv[64..127] l, hv[128..191] m, hv[192..255] q scale (FP8)
@@ -1437,6 +1458,67 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         tc_fence_before();
         named_bar_sync(kBarSoftmax, kSoftmaxThreads);  // hv[] reads done; O reads done
         if (lane == 0) mbar_arrive(bar(b_ofree));
+        // ---------------- a row cut at CTA range boundaries, in-kernel merge mode: the CTA that
+        // writes the row's last piece merges all pieces, in CTA order (the reference's stage 2,
+        // mla_decode_attention.py:1064-1137), so the result does not depend on which CTA is last
+        if (!full && a.row_done) {
+          __threadfence();  // this CTA's piece is visible before it is counted
+          named_bar_sync(kBarSoftmax, kSoftmaxThreads);
+          auto cta_of = [&](int t) {  // the non-empty range holding tile t
+            int lo = 0, hi = a.G;
+            while (hi - lo > 1) {
+              const int m = (lo + hi) >> 1;
+              if (__ldg(a.range_bounds + m) <= t) lo = m; else hi = m;
+            }
+            return lo;
+          };
+          const int c0 = cta_of(plo), c1 = cta_of(phi - 1);
+          if (tid == 0) {
+            int np = 0;
+            for (int c = c0; c <= c1; ++c) np += __ldg(a.range_bounds + c) < __ldg(a.range_bounds + c + 1);
+            const bool last = atomicAdd(a.row_done + row, 1) == np - 1;
+            if (last) __threadfence();  // the other pieces are visible before they are read
+            *fix_flag = last ? 1 : 0;
+          }
+          named_bar_sync(kBarSoftmax, kSoftmaxThreads);
+          if (*fix_flag) {
+            const int n4 = a.rank / 4, osz = dt_size(a.o_dtype);
+            for (int idx = tid; idx < R * n4; idx += kSoftmaxThreads) {
+              const int r = idx / n4, d = 4 * (idx - r * n4);
+              float m = -INFINITY;
+              for (int c = c0; c <= c1; ++c) {
+                const int b0 = __ldg(a.range_bounds + c);
+                if (b0 >= __ldg(a.range_bounds + c + 1)) continue;  // an empty range wrote nothing
+                const int sl = plo <= b0 ? 2 * c : 2 * c + 1;
+                m = fmaxf(m, __ldcg(a.part_lse + (int64_t)sl * R + r));
+              }
+              float sum = 0.f;
+              float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+              for (int c = c0; c <= c1; ++c) {
+                const int b0 = __ldg(a.range_bounds + c);
+                if (b0 >= __ldg(a.range_bounds + c + 1)) continue;
+                const int sl = plo <= b0 ? 2 * c : 2 * c + 1;
+                const float w = m == -INFINITY ? 0.f : exp2f(__ldcg(a.part_lse + (int64_t)sl * R + r) - m);
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(a.part_o + ((int64_t)sl * R + r) * a.rank + d));
+                sum += w;
+                acc.x += w * v.x;
+                acc.y += w * v.y;
+                acc.z += w * v.z;
+                acc.w += w * v.w;
+              }
+              const float inv = sum > 0.f ? 1.f / sum : 0.f;
+              const int dq = r / H;
+              uint8_t* orow = a.o + (((int64_t)row * F + dq) * a.o_sr + (int64_t)(r - dq * H) * a.o_sh + d) * osz;
+              store_from_float(orow, a.o_dtype, acc.x * inv);
+              store_from_float(orow + osz, a.o_dtype, acc.y * inv);
+              store_from_float(orow + 2 * osz, a.o_dtype, acc.z * inv);
+              store_from_float(orow + 3 * osz, a.o_dtype, acc.w * inv);
+              if (d == 0 && a.lse)
+                store_from_float(a.lse + (((int64_t)row * F + dq) * a.lse_sr + (r - dq * H)) * dt_size(a.lse_dtype),
+                                 a.lse_dtype, (m + log2f(sum)) * kLn2);
+            }
+          }
+        }
       }
       ++sidx;
       have = next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi);

@@ -402,3 +402,23 @@ def test_rank_1792_fp8(cuda_device, page):
     ref_o, ref_lse = oracle_ref(q, cache, bt, sl, rank=1792, qk_dim=2024, page=page, sm_scale=1 / 16,
                                 rms_offset=2024, rms_mode="log8", kv_fp8=True, k_scale=ks)
     compare(o, lse, ref_o, ref_lse, tol=FP8_TOL, rel_tol=2e-2)
+
+
+@pytest.mark.parametrize("merge_kernel", [False, True])
+def test_split_rows_merged_in_kernel_or_by_merge_kernel(cuda_device, merge_kernel, monkeypatch):
+    """Rows cut at CTA boundaries: merged inside the decode kernel by the CTA that writes a row's
+    last piece (many rows), or by the merge kernel (QMLA_MERGE_KERNEL, the few-rows path); both
+    against the oracle, with empty rows among them, and the in-kernel result stable across calls."""
+    if merge_kernel:
+        monkeypatch.setenv("QMLA_MERGE_KERNEL", "1")
+    g = torch.Generator().manual_seed(5)
+    lens = torch.randint(1, 3000, (48,), generator=g).tolist()
+    lens[3] = lens[17] = 0
+    cache, q, bt, sl = make_bf16_case(len(lens), 24, 768, 232, 16, lens, seed=41, device=cuda_device)
+    o, lse = _run(q, cache, bt, sl, rank=768, rms_offset=1000, page=16, o_dtype=torch.float32)
+    ref_o, ref_lse = oracle_ref(q, cache, bt, sl, rank=768, qk_dim=1000, page=16, sm_scale=1 / 16, rms_offset=1000)
+    compare(o, lse, ref_o, ref_lse, tol=BF16_TOL, rel_tol=1e-2)
+    assert torch.all(o[3] == 0) and torch.all(lse[17] == -math.inf)
+    o2, lse2 = _run(q, cache, bt, sl, rank=768, rms_offset=1000, page=16, o_dtype=torch.float32)
+    assert torch.equal(o, o2) and torch.equal(lse, lse2)  # same partition, same merge order
+    assert _status() == 0
