@@ -1163,7 +1163,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
               const int es = (!FP8 || a.rms_mode == 2) ? 2 : 1;
               auto factor = [&](int j, uint32_t bits) -> float {
                 if (FP8 && a.rms_mode == 3)  // 1 / rms = 2^(3 - code * 6/255)
-                  return gs[j] * exp2f(3.0f - (float)bits * (6.0f / 255.0f));
+                  return gs[j] * ex2_approx(3.0f - (float)bits * (6.0f / 255.0f));
                 const float rv = (!FP8 || a.rms_mode == 2)
                                      ? __bfloat162float(__ushort_as_bfloat16((uint16_t)bits))
                                      : e4m3_to_f32((uint8_t)bits) * kscale;
@@ -1205,15 +1205,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
         }
         if (tid == 0) QMLA_TR(15);
-        // PV(jt-2) must be done before P buffer pb is rewritten
-        if (jt >= 2 && ok) {
-          const uint32_t jp = jt - 2;
-          ok = mbar_wait(bar(b_odone + (jp & 1)), (jp >> 1) & 1, abort_flag, status);
-        }
-        if (named_bar_or(kBarSoftmax, kSoftmaxThreads, !ok)) {
-          ok = false;
-          break;
-        }
         if (tid == 0) QMLA_TR(10);
         // ---- logits (log2 units) and the lazy-rescale test
         bool need = false;
@@ -1228,8 +1219,19 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           x[j] = v;
           need |= v > m_ref[j] + kRescaleThreshold;
         }
-        need = named_bar_or(kBarSoftmax, kSoftmaxThreads, need);
+        // PV(jt-2) must be done before P buffer pb is rewritten
+        if (jt >= 2 && ok) {
+          const uint32_t jp = jt - 2;
+          ok = mbar_wait(bar(b_odone + (jp & 1)), (jp >> 1) & 1, abort_flag, status);
+        }
+        // One group barrier per tile: it reduces the rescale test and, folded into it, any failed
+        // wait; only when it fires does a second reduction decide uniformly whether to abort.
+        need = named_bar_or(kBarSoftmax, kSoftmaxThreads, need || !ok);
         if (tid == 0) QMLA_TR(11);
+        if (need && named_bar_or(kBarSoftmax, kSoftmaxThreads, !ok)) {
+          ok = false;
+          break;
+        }
         if (need) {
           // exact tile max per head: over this warp's 32 tokens, then the 4 sub-partitions
           float wm[NJ];
@@ -1324,16 +1326,19 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                            w[4 * c + 3]);
           } else {
             // 16 heads (16 bytes) per core-matrix row; hi columns [0, NPV), lo [NPV, 2 NPV)
+            // two elements per conversion (e4m3x2): the same round-to-nearest bytes as one at a time
             uint32_t whi[NH / 4], wlo[NH / 4];
 #pragma unroll
             for (int q4 = 0; q4 < NH / 4; ++q4) {
               whi[q4] = 0u;
               wlo[q4] = 0u;
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float v = p[q4 * 4 + e];
-                const uint8_t hi = f32_to_e4m3(v);
-                const uint8_t lo = f32_to_e4m3(v - e4m3_to_f32(hi));
+              for (int e = 0; e < 4; e += 2) {
+                const float2 v = make_float2(p[q4 * 4 + e], p[q4 * 4 + e + 1]);
+                const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(v, __NV_SATFINITE, __NV_E4M3);
+                const float2 hv2 = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(hi, __NV_E4M3)));
+                const __nv_fp8x2_storage_t lo =
+                    __nv_cvt_float2_to_fp8x2(make_float2(v.x - hv2.x, v.y - hv2.y), __NV_SATFINITE, __NV_E4M3);
                 whi[q4] |= (uint32_t)hi << (8 * e);
                 wlo[q4] |= (uint32_t)lo << (8 * e);
               }
