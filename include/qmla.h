@@ -139,9 +139,8 @@ int qmla_decode_workspace_bytes(const qmla_decode_params* p, int64_t* bytes);
 
 /* Paged MLA decode: o, lse <- softmax((q . k) / rms * sm_scale) . v per row
  * and head, reading each row's cache once.  Launches a plan kernel (a bounds
- * kernel when plan_tile_prefix is given) and the persistent decode kernel on
- * `stream`; with fewer than a quarter as many (work) rows as CTAs, also a merge
- * kernel for rows cut at CTA boundaries (otherwise the decode kernel merges them). */
+ * kernel when plan_tile_prefix is given), the persistent decode kernel and a
+ * merge kernel for rows cut at CTA boundaries on `stream`. */
 int qmla_mla_decode(const qmla_decode_params* p, void* stream);
 
 /* qmla_mla_decode for callers that cannot allocate device memory.  No counterpart in the

@@ -322,10 +322,12 @@ int make_plan_fold(const qmla_decode_params* p, Plan* pl, int fold) {
   w = align_up(w + 4 * ((int64_t)kMaxCtas + 1), 256);
   pl->ws_prefix = w;
   w = align_up(w + 4 * ((int64_t)pl->work_rows + 1), 256);
-  // Many rows (each spans at most a few CTA ranges): the CTA that finishes a row's last piece
-  // merges it, and no merge kernel runs.  Few long rows (a row over many CTAs, as in DCP
-  // shards): the merge kernel spreads each row's merge over (row, query row) blocks instead.
-  pl->row_merge = (int64_t)pl->work_rows * 4 >= G && !getenv("QMLA_MERGE_KERNEL");
+  // Rows cut at CTA boundaries are merged by the merge kernel, spread over (row, query row)
+  // blocks.  Merging them inside the decode kernel (the CTA that finishes a row's last piece
+  // merges it; test hook QMLA_ROW_MERGE, for calls with at least a quarter as many rows as CTAs)
+  // saves that launch but puts the merge on the slowest CTA's path: config 1 measured 0.647 ms
+  // against 0.621 with the merge kernel.
+  pl->row_merge = (int64_t)pl->work_rows * 4 >= G && getenv("QMLA_ROW_MERGE") != nullptr;
   pl->ws_done = w;
   w = align_up(w + 4 * (int64_t)pl->work_rows, 256);
   pl->ws_plse = w;
@@ -341,10 +343,8 @@ int make_plan_fold(const qmla_decode_params* p, Plan* pl, int fold) {
 // instead of qrows times.  Falls back to one decode row per work row where the folded shape does
 // not fit (shared memory), or when allow_fold is false (test hook QMLA_NO_FOLD: never fold).
 // Measured on B200 with 4 drafts x 8192 tokens: bf16 rank 768 x 24 heads 0.74 ms folded vs
-// 1.04 unfolded; FP8 rank 384 x 12 heads 1.04 vs 1.52; bf16 rank 384 x 12 heads 0.89 vs 1.47.
-// FP8 rank 768 x 24 heads was 1.53 vs 1.46: its 48 hi|lo query rows take
-// 96 KB of shared memory and the softmax of 48 rows per tile outweighs the halved cache reads,
-// so that shape is not folded (test hook QMLA_FOLD_ALWAYS folds it anyway).
+// 1.04 unfolded; FP8 rank 384 x 12 heads 1.04 vs 1.52; bf16 rank 384 x 12 heads 0.89 vs 1.47;
+// FP8 rank 768 x 24 heads 1.38 vs 1.48.
 int make_plan(const qmla_decode_params* p, Plan* pl, bool allow_fold = true) {
   int fold = 1;
   if (p && allow_fold && p->qrows > 1 && p->num_rows % p->qrows == 0 && !getenv("QMLA_NO_FOLD")) {
@@ -353,8 +353,6 @@ int make_plan(const qmla_decode_params* p, Plan* pl, bool allow_fold = true) {
         fold = f;
         break;
       }
-    const bool fp8 = p->kv_dtype == QMLA_DT_FP8E4M3;
-    if (fp8 && p->rank >= 768 && fold * p->num_heads > 32 && !getenv("QMLA_FOLD_ALWAYS")) fold = 1;
   }
   int rc = make_plan_fold(p, pl, fold);
   if (rc == QMLA_E_UNSUPPORTED && fold > 1) rc = make_plan_fold(p, pl, 1);

@@ -331,7 +331,6 @@ def test_mtp_rows_decoded_together(cuda_device, fp8, heads, qd, rank, rope, monk
     drafts of length 0 (a request of length 2 with 4 drafts) and tile edges."""
     lens_req = [1500, 2, 64, 900, 129, 1, 4097]
     n = len(lens_req)
-    monkeypatch.setenv("QMLA_FOLD_ALWAYS", "1")  # fold FP8 rank 768 x 24 heads too (not the default)
     if fp8:
         cache, _, bt_req, sl_req, ks = make_fp8_case(n, heads, rank, rope, 16, lens_req, seed=qd * 7 + heads,
                                                      device=cuda_device)
@@ -406,11 +405,11 @@ def test_rank_1792_fp8(cuda_device, page):
 
 @pytest.mark.parametrize("merge_kernel", [False, True])
 def test_split_rows_merged_in_kernel_or_by_merge_kernel(cuda_device, merge_kernel, monkeypatch):
-    """Rows cut at CTA boundaries: merged inside the decode kernel by the CTA that writes a row's
-    last piece (many rows), or by the merge kernel (QMLA_MERGE_KERNEL, the few-rows path); both
-    against the oracle, with empty rows among them, and the in-kernel result stable across calls."""
-    if merge_kernel:
-        monkeypatch.setenv("QMLA_MERGE_KERNEL", "1")
+    """Rows cut at CTA boundaries: merged by the merge kernel (the default), or inside the decode
+    kernel by the CTA that writes a row's last piece (test hook QMLA_ROW_MERGE); both against the
+    oracle, with empty rows among them, and each stable across calls."""
+    if not merge_kernel:
+        monkeypatch.setenv("QMLA_ROW_MERGE", "1")
     g = torch.Generator().manual_seed(5)
     lens = torch.randint(1, 3000, (48,), generator=g).tolist()
     lens[3] = lens[17] = 0
