@@ -22,7 +22,7 @@ using namespace qmla;
 namespace {
 
 constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in limit per block on sm_100
-constexpr int kMaxRing = 8;          // K / V ring slots at most (bounds the barrier area)
+constexpr int kMaxRing = 12;         // K / V ring slots at most (bounds the barrier area)
 
 struct DevInfo {
   int sms = 0;
@@ -586,6 +586,7 @@ int decode_impl(const qmla_decode_params* p, void* stream, bool allow_fold) {
 #ifdef QMLA_TRACE
   a.trace = g_trace;
   a.trace_cta = getenv("QMLA_TRACE_CTA") ? (unsigned)atoi(getenv("QMLA_TRACE_CTA")) : 0u;
+  a.trace_tid = getenv("QMLA_TRACE_TID") ? atoi(getenv("QMLA_TRACE_TID")) : 0;
 #else
   a.trace = nullptr;
 #endif

@@ -138,6 +138,7 @@ struct DecodeArgs {
   // trace[tile * 16 + event] = %globaltimer in ns.
   unsigned long long* trace;
   unsigned trace_cta;  // the CTA whose stages are traced
+  int trace_tid;       // the softmax thread whose stages are traced
 };
 
 #ifdef QMLA_TRACE
@@ -1124,7 +1125,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
         for (int j = 0; j < NJ; ++j) x[j] = 0.f;
         ok = mbar_wait(bar(b_sfull + sb), (jt / SB) & 1, abort_flag, status);
-        if (tid == 0) QMLA_TR(9);
+        if (tid == a.trace_tid) QMLA_TR(9);
         if (ok) {
           tc_fence_after();
           const uint32_t tb = tmem_base + lane_base + col_s + sb * SW + hw * NJ;
@@ -1147,14 +1148,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(b_sempty + sb));
         }
-        if (tid == 0) QMLA_TR(14);
+        if (tid == a.trace_tid) QMLA_TR(14);
         // ---- rms divisor -> per-(token, head) factor
         float f[NJ];
 #pragma unroll
         for (int j = 0; j < NJ; ++j) f[j] = gs[j];
         if (a.rms_units > 0 && ok) {
           ok = mbar_wait(bar(b_rfull + pb), (jt >> 1) & 1, abort_flag, status);
-          if (tid == 0 && a.use_tma) QMLA_TR(1);  // (event 1 is the cp.async K loader's otherwise)
+          if (tid == a.trace_tid && a.use_tma) QMLA_TR(1);  // (event 1 is the cp.async K loader's otherwise)
           if (ok) {
             if (valid) {
               // this token's staged rms tail (shared memory): one value per head, shared by a
@@ -1204,8 +1205,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             if (lane == 0) mbar_arrive(bar(b_rempty + pb));
           }
         }
-        if (tid == 0) QMLA_TR(15);
-        if (tid == 0) QMLA_TR(10);
+        if (tid == a.trace_tid) QMLA_TR(15);
+        if (tid == a.trace_tid) QMLA_TR(10);
         // ---- logits (log2 units) and the lazy-rescale test
         bool need = false;
 #pragma unroll
@@ -1227,7 +1228,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         // One group barrier per tile: it reduces the rescale test and, folded into it, any failed
         // wait; only when it fires does a second reduction decide uniformly whether to abort.
         need = named_bar_or(kBarSoftmax, kSoftmaxThreads, need || !ok);
-        if (tid == 0) QMLA_TR(11);
+        if (tid == a.trace_tid) QMLA_TR(11);
         if (need && named_bar_or(kBarSoftmax, kSoftmaxThreads, !ok)) {
           ok = false;
           break;
@@ -1359,7 +1360,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (tid == 0) QMLA_TR(12);
+        if (tid == a.trace_tid) QMLA_TR(12);
         if (lane == 0) mbar_arrive(bar(b_pfull + pb));
       }
       if (!ok) break;
