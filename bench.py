@@ -549,6 +549,38 @@ def gather_row_bytes() -> float:
     return ROW + 2 * (QK + H) + 4 + 4 / PAGE
 
 
+def run_profile_case(args) -> None:
+    """One workload's decode on cuda:0, called --warmup then --steps times with plain launches
+    (no graphs, no sub-objects, no baselines): the small cases ncu captures use.  --batch N keeps
+    the first N sequences; a GLA workload runs its first head group.  Prints one JSON line."""
+    import torch
+    from qwen_mla_vllm_b200.mla_decode_attention import run_params
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    w = workloads()[args.profile_case]
+    if args.batch and args.batch < len(w.lens):
+        w.lens = w.lens[:args.batch]
+    c = build_case(w, dev)
+    rows = c.q.shape[0]
+    o = torch.empty(rows, w.heads, w.rank, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(rows, w.heads, dtype=torch.float32, device=dev)
+    p = params_for(w, c, o, lse)
+    for _ in range(args.warmup):
+        run_params(p, dev)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        run_params(p, dev)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / args.steps
+    nbytes = w.algorithmic_bytes() / w.groups
+    print(json.dumps({"profile_case": w.key, "sequences": len(w.lens), "tokens": int(sum(w.lens)),
+                      "ms_per_call": round(ms, 4), "algorithmic_bytes": int(nbytes),
+                      "tbs": round(nbytes / ms / 1e9, 3)}))
+
+
 def run_gather(args) -> None:
     import torch
     if int(os.environ.get("WORLD_SIZE", "1")) != 1:
@@ -1151,11 +1183,15 @@ def main():
                     help=argparse.SUPPRESS)  # child process of triton_child()
     ap.add_argument("--batch", type=int, default=None,
                     help="first N sequences of config1 (smaller cases for ncu captures; default: all 64)")
+    ap.add_argument("--profile-case", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default=None,
+                    help="only this workload's decode, plain launches (ncu captures); --batch applies")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.triton_baseline:
         run_triton_child(args)
+    elif args.profile_case:
+        run_profile_case(args)
     elif args.workload == "gather":
         if args.impl == "reference":
             raise SystemExit("--workload gather has no reference arm; its line carries cpu_baseline")

@@ -60,23 +60,24 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-using MapKey = std::tuple<const void*, int, int, int, int64_t, int64_t, int64_t, int>;
+using MapKey = std::tuple<const void*, int, int, int, int64_t, int64_t, int64_t, int, int>;
 std::map<MapKey, CacheMaps> g_maps;
 
-// The decode kernel's two maps over the paged cache (CacheMaps in qmla_decode.cuh):
+// The decode kernel's three maps over the paged cache (CacheMaps in qmla_decode.cuh):
 //   chunk: 3-D (row element, token in page, page), box = one 128-byte column x `run`
 //          tokens; the row extent is the QK width, so columns past it (rms tail,
 //          padding) are zero-filled;
 //   pair:  5-D (element of a 128-byte column, token in an 8-token group, column,
 //          8-token group in the page, page), box = two columns x `run` tokens, which
 //          lands as [8-token group][column][token][128 B]; the column extent counts the
-//          full columns only.
-// Pages outside [0, num_pages) are zero-filled by both.
-int cache_tensor_map(const qmla_decode_params* p, int run, CacheMaps* out) {
+//          full columns only;
+//   vrows: the pair map's view with box = `vcols` columns x 16 tokens (V slots).
+// Pages outside [0, num_pages) are zero-filled by all three.
+int cache_tensor_map(const qmla_decode_params* p, int run, int vcols, CacheMaps* out) {
   const bool fp8 = p->kv_dtype == QMLA_DT_FP8E4M3;
   const int es = fp8 ? 1 : 2;
   MapKey key{p->kv_cache, p->kv_dtype, p->qk_dim, p->page_size, p->kv_num_pages,
-             p->kv_stride_page, p->kv_stride_token, run};
+             p->kv_stride_page, p->kv_stride_token, run, vcols};
   {
     std::lock_guard<std::mutex> lk(g_mu);
     auto it = g_maps.find(key);
@@ -109,6 +110,18 @@ int cache_tensor_map(const qmla_decode_params* p, int run, CacheMaps* out) {
     cuuint32_t box[5] = {(cuuint32_t)(128 / es), 8, 2, (cuuint32_t)(run / 8), 1};
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     CUresult r = fn(&m.pair, dt, 5, const_cast<void*>(p->kv_cache), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return QMLA_E_ALIGNMENT;
+  }
+  {
+    const int full_chunks = p->qk_dim * es / 128;
+    cuuint64_t dims[5] = {(cuuint64_t)(128 / es), 8, (cuuint64_t)full_chunks,
+                          (cuuint64_t)(p->page_size / 8), (cuuint64_t)p->kv_num_pages};
+    cuuint64_t strides[4] = {(cuuint64_t)tok_b, 128, (cuuint64_t)(8 * tok_b), (cuuint64_t)page_b};
+    cuuint32_t box[5] = {(cuuint32_t)(128 / es), 8, (cuuint32_t)vcols, 2, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = fn(&m.vrows, dt, 5, const_cast<void*>(p->kv_cache), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return QMLA_E_ALIGNMENT;
@@ -161,7 +174,10 @@ struct Plan {
   int fold, R, work_rows;  // decode rows folded into one work row, its query rows, work rows
   int npv, nb, nqk;
   int use_tma, run;
-  int n_qk_slots, n_sub_qk, n_full_chunks, cps, v_groups;
+  int n_qk_slots, n_sub_qk, n_full_chunks, cps;
+  int v_tma;               // V slots by TMA boxes
+  int v_blocks;            // V by TMA: output blocks per V slot
+  uint32_t v_slot_bytes;   // bytes of a V slot
   int qk_bytes, row_bytes;
   int rms_bytes, rms_base_b, rms_units, rms_skip, pf_bytes;
   int G;
@@ -235,17 +251,15 @@ int make_plan_fold(const qmla_decode_params* p, Plan* pl, int fold) {
     end = std::min<int64_t>(align_up(end, 16), p->kv_stride_token * es);
     pl->pf_bytes = (int)end;
   }
-  // K slots hold one or two 128-byte column chunks of each of the tile's 128 tokens.
-  // Two (paired layout, 4 KB TMA boxes) with three V groups measured fastest for the bf16
-  // rank-768 shape (config 1: 3.91 vs 3.74 TB/s); one chunk per slot with two V warps
-  // sharing each slot was faster for the smaller GLA head group (2.90 vs 2.46) and for
-  // FP8 (2.70 vs 2.63), so those keep it.
+  // K slots hold one or two 128-byte column chunks of each of the tile's 128 tokens.  Two
+  // (paired layout, 4 KB TMA boxes) for rank 768 with up to 32 query rows: one lane-issued
+  // TMA box costs ~70 ns whatever its size up to 4 KB, so 2 KB boxes held the K stream to
+  // ~35 GB/s per SM against ~56 GB/s with 4 KB boxes (B200, boxes of random pages).
   pl->n_sub_qk = (pl->qk_bytes + 127) / 128;
   pl->n_full_chunks = pl->qk_bytes / 128;
-  bool paired = pl->use_tma && !fp8 && nb == 6 && pl->nqk <= 32;
+  bool paired = pl->use_tma && nb == 6 && pl->nqk <= 32;
   if (getenv("QMLA_NO_PAIR")) paired = false;  // test hook: the one-column layout
   pl->cps = paired ? 2 : 1;
-  pl->v_groups = paired ? 3 : 1;
   pl->n_qk_slots = (pl->n_sub_qk + pl->cps - 1) / pl->cps;
   if (pl->n_sub_qk > kMaxQkChunks) return QMLA_E_UNSUPPORTED;
   // 16-byte vector loads of q rows (bf16 only; element strides in 2-byte units)
@@ -266,7 +280,6 @@ int make_plan_fold(const qmla_decode_params* p, Plan* pl, int fold) {
 
   // shared memory map: K ring, V ring, Q, 2 P buffers, 2 rms staging buffers, misc
   const uint32_t kslot = 16384u * (uint32_t)pl->cps;  // 128 tokens x cps 128-byte columns
-  const uint32_t vslot = fp8 ? 8192u : 16384u;  // 64 tokens x 128 dims
   const int q_rows = fp8 ? 2 * pl->nqk : pl->nqk;
   pl->q_chunk = (uint32_t)((q_rows + 7) / 8 * 1024);
   const uint32_t q_bytes = pl->q_chunk * pl->n_sub_qk;
@@ -275,21 +288,51 @@ int make_plan_fold(const qmla_decode_params* p, Plan* pl, int fold) {
   const uint32_t rms_smem = (uint32_t)(2 * kTile * 16 * pl->rms_units);  // two staging buffers
   const uint32_t fixed = q_bytes + 2 * pl->p_bytes + misc_bytes + rms_smem + 1024 /*align slack*/;
   const int budget = std::min(di.max_smem, kMaxDynSmem) - (int)fixed;
+  // V slots.  By TMA (bf16 caches with one-column K slots): one PV K step of tokens (16) x
+  // v_blocks output blocks, 4 KB per block, filled by one box per 16 tokens; v_blocks = the
+  // largest divisor of the block count with slots of at most 24 KB of which two fit beside
+  // 64 KB of K slots (else beside one K slot).  By cp.async: 64 tokens x one block, filled by
+  // three warps in turn (paired K slots) or two warps sharing each slot.  Measured on B200
+  // against the cp.async fills: GLA rank 384 x 12 heads (config 3) 0.61 vs 0.74 ms per group;
+  // config 1 (paired) 0.65 vs 0.63, e4m3 config 2 (48 query rows, 2 KB K boxes) 1.57 vs 1.35:
+  // their K boxes queue behind the V boxes in the SM's TMA unit.
   // The V groups take the V slots in turn (slot n: group n % v_groups).  With at least as
   // many slots as groups, a group's wait for slot n's position to be free comes after its
   // own fill of slot n - v_groups, so the position is never two phases behind (a parity
   // wait would then pass early; with fewer slots than groups calls hung until the 2 s
-  // wait limit).  Two slots at least, so a load overlaps the MMAs of the previous block.
-  const int nv_min = std::max(2, pl->v_groups);
+  // wait limit).  Two slots at least, so a load overlaps the MMAs of the previous slot.
+  pl->v_tma = pl->use_tma && !fp8 && !paired;
+  // test hook: V copied by cp.async where the default is TMA boxes (the kernels that take
+  // boxes are built for bf16 with one-column K slots only)
+  if (const char* e = getenv("QMLA_V_TMA")) pl->v_tma = pl->v_tma && atoi(e) != 0;
+  const int nv_min = pl->v_tma ? 2 : std::max(2, paired ? 3 : 1);
+  pl->v_blocks = nb;
+  uint32_t vslot = fp8 ? 8192u : 16384u;
+  int v_per_tile = 2 * nb;  // V slots per tile
+  if (pl->v_tma) {
+    int vb = 0;
+    for (int kr : {std::max<int>((int)kslot, 65536), (int)kslot})
+      for (int d = nb; d >= 1 && !vb; --d)
+        if (nb % d == 0 && 4096 * d <= 24576 && budget >= kr + nv_min * 4096 * d) vb = d;
+    if (const char* e = getenv("QMLA_VB")) {  // test hook: blocks per V slot (a legal divisor)
+      const int d = atoi(e);
+      if (d >= 1 && d <= nb && nb % d == 0 && budget >= (int)kslot + nv_min * 4096 * d) vb = d;
+    }
+    if (!vb) return QMLA_E_UNSUPPORTED;
+    pl->v_blocks = vb;
+    vslot = 4096u * (uint32_t)vb;
+    v_per_tile = (kTile / (fp8 ? 32 : 16)) * (nb / vb);
+  }
+  pl->v_slot_bytes = vslot;
   if (budget < (int)(kslot + nv_min * vslot)) return QMLA_E_UNSUPPORTED;
   // K ring: the HBM stream (bandwidth x latency), ~55% of the rings; V ring: L2 re-reads for PV
   const int nk_max = (budget - nv_min * (int)vslot) / (int)kslot;
   int nk = std::min(((budget * 11 / 20) + (int)kslot - 1) / (int)kslot, 3 * pl->n_qk_slots);
-  if (paired) nk = 2;  // 64 KB of K, the rest for V (swept: 2 x 32 KB + 5 x 16 KB best)
+  if (paired) nk = 2;  // 64 KB of K, the rest for V
   nk = std::max(1, std::min({nk, nk_max, kMaxRing}));
   // test hooks: QMLA_NK / QMLA_NV override the ring sizes (clamped to legal values)
   if (const char* e = getenv("QMLA_NK")) nk = std::max(1, std::min({atoi(e), nk_max, kMaxRing}));
-  int nv = std::min({(budget - nk * (int)kslot) / (int)vslot, 2 * nb, kMaxRing});
+  int nv = std::min({(budget - nk * (int)kslot) / (int)vslot, 2 * v_per_tile, kMaxRing});
   if (const char* e = getenv("QMLA_NV")) nv = std::min(atoi(e), nv);
   nv = std::max(nv, nv_min);
   if (nk * (int)kslot + nv * (int)vslot > budget) return QMLA_E_UNSUPPORTED;
@@ -419,12 +462,13 @@ int launch_decode_fp(int nb, int nqk, const CacheMaps& maps, const DecodeArgs& a
   return QMLA_E_UNSUPPORTED;
 }
 
-// paired K slots: instantiated for the bf16 rank-768 shape only (the planner's choice)
+// paired K slots: instantiated for rank 768 (the planner's choice)
 int launch_decode(bool fp8, bool paired, int nb, int nqk, const CacheMaps& maps,
                   const DecodeArgs& a, uint32_t smem, cudaStream_t st) {
   if (paired) {
-    if (fp8 || nb != 6) return QMLA_E_UNSUPPORTED;
-    return launch_decode_nb<false, 6, true>(nqk, maps, a, smem, st);
+    if (nb != 6) return QMLA_E_UNSUPPORTED;
+    return fp8 ? launch_decode_nb<true, 6, true>(nqk, maps, a, smem, st)
+               : launch_decode_nb<false, 6, true>(nqk, maps, a, smem, st);
   }
   return fp8 ? launch_decode_fp<true>(nb, nqk, maps, a, smem, st)
              : launch_decode_fp<false>(nb, nqk, maps, a, smem, st);
@@ -579,6 +623,9 @@ int decode_impl(const qmla_decode_params* p, void* stream, bool allow_fold) {
   a.nv = pl.nv;
   a.off_q = pl.off_q;
   a.q_chunk_bytes = pl.q_chunk;
+  a.v_tma = pl.v_tma;
+  a.v_blocks = pl.v_blocks;
+  a.v_slot_bytes = pl.v_slot_bytes;
   a.off_p = pl.off_p;
   a.p_bytes = pl.p_bytes;
   a.off_rms = pl.off_rms;
@@ -595,7 +642,7 @@ int decode_impl(const qmla_decode_params* p, void* stream, bool allow_fold) {
   CacheMaps maps;
   memset(&maps, 0, sizeof(maps));
   if (pl.use_tma) {
-    rc = cache_tensor_map(p, pl.run, &maps);
+    rc = cache_tensor_map(p, pl.run, pl.v_blocks * (p->kv_dtype == QMLA_DT_FP8E4M3 ? 1 : 2), &maps);
     if (rc != QMLA_OK) return rc;
   }
   int32_t* bounds = reinterpret_cast<int32_t*>(ws + pl.ws_bounds);

@@ -9,13 +9,15 @@
 //   warp  8     K loads: TMA boxes (two 128-byte columns x a run of tokens of one
 //               page) into the K ring; warp 9 stages the rms tail.  Page sizes that
 //               are not multiples of 16 use 16-byte cp.async gathers from warps 8-10
-//   warps 10, 11, 15  V loads: re-read the tile's latent columns (L2-resident by
-//               then) into the V ring once QK of the tile has finished (warps 11 and
-//               15 in cp.async mode), one whole V slot per warp in turn
+//   warps 10, 11, 15  V loads: re-read the tile's latent columns (L2-resident by then)
+//               into the V ring once QK of the tile has finished.  One-column bf16 K slots:
+//               warp 10 alone, one TMA box per 16 tokens carrying every column of the slot's
+//               output blocks.  Otherwise 16-byte cp.async copies: with paired K slots
+//               warps 10, 11 and 15 fill whole slots in turn, else two warps share each slot
 //   warps 12-13 QK issuers (tcgen05), one S partial each; warp 12 owns TMEM
-//   warp  14    PV issuer (tcgen05), all 128-dim output blocks of a tile in order
-//               (two issuers interleaving blocks were 8% slower: the tensor pipe
-//               pays for every switch between accumulators)
+//   warp  14    PV issuer (tcgen05): per V slot, one MMA into each of the slot's
+//               128-dim output blocks (two for e4m3: P's hi and lo terms); narrow MMAs
+//               measured ~43 cycles each whether they hit one accumulator or rotate
 // Per 128-token tile:
 //   S^T[128 tok, heads] = K_tile . Q^T     tcgen05 M=128, K-major A and B
 //   softmax over tokens with the per-(token, head) rms divisor, base 2, lazy
@@ -134,6 +136,9 @@ struct DecodeArgs {
   int G;
   // shared-memory layout (byte offsets from the 1024-aligned base)
   uint32_t off_kring, nk, off_vring, nv, off_q, q_chunk_bytes, off_p, p_bytes, off_rms, off_misc;
+  int v_tma;              // 1: V slots by TMA boxes (needs use_tma); 0: by 16-byte cp.async
+  int v_blocks;           // V by TMA: 128-dim output blocks per V slot (a divisor of rank / 128)
+  uint32_t v_slot_bytes;  // V by TMA: bytes of a V slot (4 KB per output block)
   // Optional stage timestamps of CTA 0 (builds with -DQMLA_TRACE only):
   // trace[tile * 16 + event] = %globaltimer in ns.
   unsigned long long* trace;
@@ -336,10 +341,14 @@ __device__ __forceinline__ uint64_t token_row_addr(const DecodeArgs& a, const in
 //   pair:  5-D (element of a 128-byte column, token in an 8-token group, column,
 //          8-token group in the page, page); box = two columns x run tokens, landing in
 //          the paired slot layout.  Its column extent counts only full columns.
-// Pages outside [0, num_pages) are zero-filled by both.
+//   vrows: the pair map's 5-D view with box = v_blocks output blocks (their 128-byte
+//          columns) x 16 tokens, landing as [8-token group][column][token][128 B]: the V
+//          slot layout the PV MMA reads directly.
+// Pages outside [0, num_pages) are zero-filled by all three.
 struct CacheMaps {
   CUtensorMap chunk;
   CUtensorMap pair;
+  CUtensorMap vrows;
 };
 
 // With paired slots (PAIR), K slot s uses the plain layout (loaded column by column
@@ -356,9 +365,8 @@ __device__ __forceinline__ bool slot_plain(const DecodeArgs& a, int s) {
 }
 
 // ---------------------------------------------------------------- the kernel
-// PAIR: K slots of two columns (paired layout, 4 KB TMA boxes) and V slots filled by the
-// three V warps in turn; chosen for the bf16 rank-768 shape.  Otherwise one column per K
-// slot and two V warps sharing every V slot (see the planner for the measurements).
+// PAIR: K slots of two columns (paired layout, 4 KB TMA boxes), chosen for rank 768 with up to
+// 32 query rows.  Otherwise one column per K slot.
 template <bool FP8, int NB, int NQK, bool PAIR>
 __global__ void __launch_bounds__(kNumThreads, 1)
     mla_decode_kernel(const __grid_constant__ CacheMaps maps, const DecodeArgs a) {
@@ -368,14 +376,21 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   // chunk and only produce S columns nobody reads); the hi|lo q rows for FP8.
   constexpr int NQKM = FP8 ? 2 * NQK : NPV;
   // K ring slot: 128 tokens x two 128-byte column chunks of the row (the layout is in the
-  // file header).  V ring slot: 64 tokens x one 128-dim output block.
+  // file header).  V ring slot, TMA mode: kVTokT tokens (one PV K step) x v_blocks output
+  // blocks, [8-token group][column][token][128 B]; cp.async mode: 64 tokens x one block.
   constexpr int kKChunkBytes = 16384;             // one column chunk of 128 tokens
   constexpr int CPS = PAIR ? 2 : 1;               // column chunks per K slot
   constexpr uint32_t kKSlotBytes = kKChunkBytes * CPS;
-  constexpr int VG = PAIR ? 3 : 1;                // V slot groups (see the V loader)
-  constexpr int kVSlotBytes = FP8 ? 8192 : 16384;
+  // V by TMA boxes: built into the bf16 one-column-K kernels only (the planner's choice there);
+  // the other kernels keep only the cp.async fills.
+  constexpr bool kVBoxes = !FP8 && !PAIR;
+  constexpr int kCpb = FP8 ? 1 : 2;               // 128-byte columns per 128-dim output block
+  constexpr int kVTokT = FP8 ? 32 : 16;           // tokens per V slot (TMA mode)
+  constexpr int kVStepsT = kTile / kVTokT;        // token steps per tile (TMA mode)
+  constexpr int VG = PAIR ? 3 : 1;                // V slot groups when V is copied (see the V loader)
+  constexpr int kVSlotBytes = FP8 ? 8192 : 16384;  // cp.async mode
   constexpr int kVUnits = (FP8 ? 1 : 2) * 8;      // 16-byte units per token per V slot
-  constexpr int kVTok = 64;                       // tokens per V slot (two per block and tile)
+  constexpr int kVTok = 64;                       // tokens per V slot (cp.async mode)
   constexpr int OW = NPV;                         // TMEM columns per O block
   constexpr int SWP = FP8 ? 2 * NPV : NPV;        // TMEM columns per S partial (hi|lo for FP8)
   // S partials: one per QK issuer (two issuers, each every other K step, when TMEM holds two
@@ -473,7 +488,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       mbar_init(bar(b_kempty + i), KP);
     }
     for (uint32_t i = 0; i < nv; ++i) {
-      mbar_init(bar(b_vfull + i), VG == 3 ? 32 : 64);  // the warps that fill a slot
+      mbar_init(bar(b_vfull + i), (kVBoxes && a.v_tma) ? 1 : VG == 3 ? 32 : 64);  // one TMA arm, or the copying warps
       mbar_init(bar(b_vempty + i), 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -734,8 +749,101 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
     }
     if (!ok) asm volatile("cp.async.wait_all;" ::: "memory");
-  } else if (warp == kWarpV || warp == kWarpVX || (a.use_tma && warp == kWarpK + 2)) {
+  } else if (kVBoxes && a.v_tma && warp == kWarpK + 2) {
+    // ====================================================== V loads by TMA (from L2)
+    // Once QK(jt) has consumed the tile, its latent columns are in L2.  A V slot holds one PV
+    // K step of tokens (32 e4m3 / 16 bf16) x v_blocks output blocks; one box per 16 tokens of
+    // a page carries all of the slot's 128-byte columns (v_blocks x 2 or 4 KB), so a tile
+    // takes 8 boxes per block group instead of a 16-byte copy per (token, column unit):
+    // 16-byte cp.async fills ran at ~20 GB/s per SM, TMA boxes of 12-24 KB from L2 at
+    // 115-133 GB/s.  Lanes 0-7 hold the page and 8-token group of the tile's 16-token runs.
+    const uint64_t pol = policy_evict_first();  // the latent's last use in this call
+    const int vb = a.v_blocks, nbg = NB / vb;
+    const int cv = vb * kCpb;                   // 128-byte columns per slot row group
+    constexpr int kBoxTok = 16;
+    constexpr int kBoxes = kVTokT / kBoxTok;    // boxes per slot: 2 (e4m3) or 1 (bf16)
+    const uint32_t box_bytes = (uint32_t)(kBoxTok * cv * 128);
+    if (lane == 0) prefetch_tmap(&maps.vrows);
+    SegCursor cur{row0, range_lo, range_hi};
+    int row, k0, k1, plo, phi;
+    uint32_t jt = 0, armed = 0;
+    Ring r;
+    bool ok = true;
+    while (ok && next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi)) {
+      const int L = work_len(a.seq_lens, a.fold, row);
+      const int32_t* bt = work_bt(a, row);
+      for (int k = k0; k < k1 && ok; ++k, ++jt) {
+        int pg = -1, gy = 0;  // page (-1: past the row end, loads zeros) and 8-token group
+        if (lane < kTile / kBoxTok) {
+          const int tok = k * kTile + lane * kBoxTok;
+          if (tok < L) {
+            pg = __ldg(bt + tok / a.page_size);
+            gy = (tok % a.page_size) / 8;
+          }
+        }
+        if (lane == 0)
+          ok = mbar_wait(bar(b_kdone + (jt % kKdoneDepth)), (jt / kKdoneDepth) & 1, abort_flag,
+                         status);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (lane == 0) QMLA_TR(6);
+        for (int vs = 0; vs < kVStepsT * nbg && ok; ++vs) {  // token step vs / nbg, block group vs % nbg
+          const int ts = vs / nbg, bg = vs - ts * nbg;
+          // A 16-token run that straddles the row end would bring the page's stale rows past
+          // L, and P = 0 times a NaN there is NaN: such a slot is copied 16 bytes per lane
+          // instead, zero-filled past L (at most one slot per row).
+          const int t0 = k * kTile + ts * kVTokT;
+          const bool ragged = (L & 15) != 0 && L > t0 && L < t0 + kVTokT;
+          const uint32_t slot = vring + r.idx * a.v_slot_bytes;
+          if (lane == 0) {
+            ok = mbar_wait(bar(b_vempty + r.idx), r.ph ^ 1, abort_flag, status);
+            if (ok && !ragged) mbar_expect_tx(bar(b_vfull + r.idx), a.v_slot_bytes);
+          }
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (ok && !ragged) {
+            const int run = ts * kBoxes + (lane < kBoxes ? lane : 0);
+            const int mypg = __shfl_sync(0xffffffffu, pg, run);
+            const int myg = __shfl_sync(0xffffffffu, gy, run);
+            if (lane < kBoxes)
+              tma_load_5d(slot + lane * box_bytes, &maps.vrows, 0, 0, bg * cv, myg, mypg,
+                          bar(b_vfull + r.idx), pol);
+            ++armed;
+          } else if (ok) {
+            // unit i: token i / (cv * 8) of the slot, column (i / 8) % cv, 16-byte unit i % 8,
+            // at the slot layout's swizzled position
+            for (int i = lane; i < kVTokT * cv * 8; i += 32) {
+              const int tl = i / (cv * 8), rem = i - tl * (cv * 8), c = rem >> 3, u = rem & 7;
+              const uint64_t src = token_row_addr(a, bt, L, k, ts * kVTokT + tl);
+              const int colb = (bg * cv + c) * 128 + u * 16;
+              cp_async_16_hint(slot + (uint32_t)((tl >> 3) * cv * 1024 + c * 1024 + (tl & 7) * 128 +
+                                                 ((u ^ (tl & 7)) << 4)),
+                               src ? reinterpret_cast<const void*>(src + colb) : a.cache,
+                               src ? 16u : 0u, pol);
+            }
+            cp_async_mbar_arrive_extra(bar(b_vfull + r.idx));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(b_vfull + r.idx));  // the slot's expected arrival
+          }
+          if (lane == 0 && vs < 16) QMLA_TRS(3, vs);
+          r.next(nv);
+        }
+        if (lane == 0) QMLA_TR(13);
+      }
+    }
+    // After an abort: wait (bounded) for the boxes already issued, and for the copies.
+    if (!ok) {
+      asm volatile("cp.async.wait_all;" ::: "memory");
+      if (lane == 0) {
+        for (uint32_t p = armed > nv ? armed - nv : 0u; p < armed; ++p) {
+          volatile int never = 0;
+          mbar_wait(bar(b_vfull + p % nv), (p / nv) & 1, &never, nullptr, 20000000ull);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (!(kVBoxes && a.v_tma) && (warp == kWarpV || warp == kWarpVX || (a.use_tma && warp == kWarpK + 2))) {
     // ====================================================== V loads by cp.async (from L2)
+    // (e4m3 caches and paired bf16 K slots: their K boxes would queue behind V boxes in the
+    // SM's TMA unit; page sizes that rule TMA out)
     // V slot number n (counted over the CTA's whole run) is filled by group n % v_groups.
     // v_groups == 3 (TMA mode): warps 10, 11 and 15 each fill whole slots in turn (more
     // copies in flight; the config-1 shape gains).  v_groups == 1: warps 10 and 11 (TMA
@@ -889,7 +997,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       SegCursor cur{row0, range_lo, range_hi};
       int row, k0, k1, plo, phi;
       uint32_t jt = 0, sidx = 0;
-      Ring r;  // V ring position (slots in order: block-major, then token half)
+      Ring r;  // V ring position (V by TMA: token-step-major; cp.async: block-major, then token half)
       bool ok = true;
       while (ok && next_segment(a.tile_prefix, cur, row, k0, k1, plo, phi)) {
         for (int k = k0; k < k1 && ok; ++k, ++jt) {
@@ -901,32 +1009,63 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           // B = P^T (K = tokens, N = heads), MN-major, no swizzle: core matrix =
           //   8 tokens x 16 bytes; LBO = token-group stride, SBO = head-block stride
           const uint64_t bd0 = make_sdesc(pbuf + pb * a.p_bytes, 16 * NPV, 128, 0);
-          for (int bh = 0; bh < 2 * NB && ok; ++bh) {  // block bh/2, token half bh%2
-            const int b = bh >> 1, hh = bh & 1;
-            const uint32_t vidx = r.idx, vph = r.ph;
-            r.next(nv);
-            ok = mbar_wait(bar(b_vfull + vidx), vph, abort_flag, status);
-            if (!ok) break;
-            fence_proxy_async_smem();  // cp.async-written V slot -> tensor-core reads
-            tc_fence_after();
-            // A = V^T (M = 128 dims, K = tokens), MN-major, 128-byte swizzle:
-            //   LBO = stride between 64-dim halves (bf16), SBO = 8-token group stride
-            const uint64_t ad0 = make_sdesc(vring + vidx * kVSlotBytes, 8192, 1024, 2);
-            const uint32_t d_o = tmem_base + col_o + b * OW;
-#pragma unroll
-            for (int ks = 0; ks < kPvSteps; ++ks) {
-              const uint64_t ad = ad0 + (uint64_t)(ks * (kPvAStep >> 4));
-              const uint64_t bd = bd0 + (uint64_t)((hh * kPvHalfB + ks * kPvBStep) >> 4);
-              const uint32_t acc = (k == k0 && hh == 0 && ks == 0) ? 0u : 1u;
-              if constexpr (FP8) {
-                // P = P_hi + P_lo: the lo half starts NPV/16 head blocks further on
-                tc_mma_f8_ss(d_o, ad, bd, idesc, acc);
-                tc_mma_f8_ss(d_o, ad, bd + (uint64_t)((8 * NPV) >> 4), idesc, 1u);
-              } else {
-                tc_mma_f16_ss(d_o, ad, bd, idesc, acc);
+          if (kVBoxes && a.v_tma) {
+            // V slots of one token step x v_blocks blocks (TMA layout): A = block b of the slot,
+            // MN-major SW128, its two 64-dim halves (bf16) 1 KB apart, 8-token groups
+            // (columns per slot) KB apart; B = the step's rows of P^T.
+            const int vb = a.v_blocks, nbg = NB / vb;
+            const uint32_t sbo = (uint32_t)(vb * kCpb * 1024);
+            for (int vs = 0; vs < kVStepsT * nbg && ok; ++vs) {
+              const int ts = vs / nbg, bg = vs - ts * nbg;
+              const uint32_t vidx = r.idx, vph = r.ph;
+              r.next(nv);
+              ok = mbar_wait(bar(b_vfull + vidx), vph, abort_flag, status);
+              if (!ok) break;
+              fence_proxy_async_smem();  // the row-end slot is written by cp.async
+              tc_fence_after();
+              const uint32_t slot = vring + vidx * a.v_slot_bytes;
+              const uint64_t bd = bd0 + (uint64_t)((ts * (kVTokT / 8) * 16 * NPV) >> 4);
+              const uint32_t acc = (k == k0 && ts == 0) ? 0u : 1u;
+              for (int b = 0; b < vb; ++b) {
+                const uint64_t ad = make_sdesc(slot + (uint32_t)(b * kCpb * 1024), 1024, sbo, 2);
+                const uint32_t d_o = tmem_base + col_o + (uint32_t)((bg * vb + b) * OW);
+                if constexpr (FP8) {
+                  tc_mma_f8_ss(d_o, ad, bd, idesc, acc);
+                  tc_mma_f8_ss(d_o, ad, bd + (uint64_t)((8 * NPV) >> 4), idesc, 1u);
+                } else {
+                  tc_mma_f16_ss(d_o, ad, bd, idesc, acc);
+                }
               }
+              tc_commit(bar(b_vempty + vidx));
             }
-            tc_commit(bar(b_vempty + vidx));
+          } else {
+            for (int bh = 0; bh < 2 * NB && ok; ++bh) {  // block bh/2, token half bh%2
+              const int b = bh >> 1, hh = bh & 1;
+              const uint32_t vidx = r.idx, vph = r.ph;
+              r.next(nv);
+              ok = mbar_wait(bar(b_vfull + vidx), vph, abort_flag, status);
+              if (!ok) break;
+              fence_proxy_async_smem();  // cp.async-written V slot -> tensor-core reads
+              tc_fence_after();
+              // A = V^T (M = 128 dims, K = tokens), MN-major, 128-byte swizzle:
+              //   LBO = stride between 64-dim halves (bf16), SBO = 8-token group stride
+              const uint64_t ad0 = make_sdesc(vring + vidx * kVSlotBytes, 8192, 1024, 2);
+              const uint32_t d_o = tmem_base + col_o + b * OW;
+#pragma unroll
+              for (int ks = 0; ks < kPvSteps; ++ks) {
+                const uint64_t ad = ad0 + (uint64_t)(ks * (kPvAStep >> 4));
+                const uint64_t bd = bd0 + (uint64_t)((hh * kPvHalfB + ks * kPvBStep) >> 4);
+                const uint32_t acc = (k == k0 && hh == 0 && ks == 0) ? 0u : 1u;
+                if constexpr (FP8) {
+                  // P = P_hi + P_lo: the lo half starts NPV/16 head blocks further on
+                  tc_mma_f8_ss(d_o, ad, bd, idesc, acc);
+                  tc_mma_f8_ss(d_o, ad, bd + (uint64_t)((8 * NPV) >> 4), idesc, 1u);
+                } else {
+                  tc_mma_f16_ss(d_o, ad, bd, idesc, acc);
+                }
+              }
+              tc_commit(bar(b_vempty + vidx));
+            }
           }
           if (ok) tc_commit(bar(b_odone + pb));
           QMLA_TR(8);

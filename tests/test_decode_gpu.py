@@ -79,15 +79,17 @@ def test_baseline_config0(cuda_device):
 
 
 @pytest.mark.parametrize("page", [1, 8, 16, 64, 400, 784])
-@pytest.mark.parametrize("path", ["tma", "tma_one_column", "cp_async"])
+@pytest.mark.parametrize("path", ["tma", "tma_one_column", "tma_one_column_v_copied", "cp_async"])
 def test_pages_paths_ragged(cuda_device, page, path, monkeypatch):
-    """Every page size on every load path (TMA with the paired two-column K slots this shape
-    gets by default, TMA with one-column slots, cp.async), ragged lengths including 0, 1 and
-    tile edges."""
+    """Every page size on every load path (TMA K in the paired two-column slots this shape gets
+    by default, with V copied 16 bytes at a time; one-column K slots, whose bf16 V comes by TMA
+    boxes; the same with V copied; cp.async), ragged lengths including 0, 1 and tile edges."""
     if path == "cp_async":
         monkeypatch.setenv("QMLA_NO_TMA", "1")
-    if path == "tma_one_column":
+    if path.startswith("tma_one_column"):
         monkeypatch.setenv("QMLA_NO_PAIR", "1")
+    if path == "tma_one_column_v_copied":
+        monkeypatch.setenv("QMLA_V_TMA", "0")
     lens = [0, 1, 63, 64, 65, 1000, 2049, 130]
     cache, q, bt, sl = make_bf16_case(len(lens), 24, 768, 232, page, lens, seed=page, device=cuda_device)
     o, lse = _run(q, cache, bt, sl, rank=768, rms_offset=1000, page=page)
@@ -126,8 +128,14 @@ def test_head_and_rank_shapes(cuda_device, heads, rank, rope):
     compare(o, lse, ref_o, ref_lse, tol=BF16_TOL, rel_tol=1e-2)
 
 
-def test_nan_past_row_end_is_never_read(cuda_device):
-    """Cache rows past a row's length (inside its last page) hold NaN: outputs stay exact."""
+@pytest.mark.parametrize("path", ["paired_k", "v_boxes", "v_copied"])
+def test_nan_past_row_end_is_never_read(cuda_device, path, monkeypatch):
+    """Cache rows past a row's length (inside its last page) hold NaN: outputs stay exact on
+    every V path (a V box straddling the row end must not carry them into P = 0 times NaN)."""
+    if path != "paired_k":
+        monkeypatch.setenv("QMLA_NO_PAIR", "1")  # one-column K slots: V by TMA boxes
+    if path == "v_copied":
+        monkeypatch.setenv("QMLA_V_TMA", "0")
     lens = [37, 100, 64]
     cache, q, bt, sl = make_bf16_case(len(lens), 24, 768, 232, 16, lens, seed=5, device=cuda_device)
     for b, L in enumerate(lens):
@@ -141,6 +149,23 @@ def test_nan_past_row_end_is_never_read(cuda_device):
     ref_o, ref_lse = oracle_ref(q, cache, bt, sl, rank=768, qk_dim=1000, page=16, sm_scale=1 / 16, rms_offset=1000)
     compare(o, lse, ref_o, ref_lse, tol=BF16_TOL, rel_tol=1e-2)
 
+
+
+def test_fp8_nan_past_row_end_is_never_read(cuda_device):
+    """e4m3 NaN bytes (0x7f) in the rows past each row's length: outputs stay exact."""
+    lens = [37, 100, 64, 300]
+    cache, q, bt, sl, ks = make_fp8_case(len(lens), 24, 768, 232, 16, lens, seed=9, device=cuda_device)
+    ref_o, ref_lse = oracle_ref(q, cache, bt, sl, rank=768, qk_dim=1000, page=16, sm_scale=1 / 16,
+                                rms_offset=1000, rms_mode="log8", kv_fp8=True, k_scale=ks)
+    raw = cache.view(torch.uint8)
+    for b, L in enumerate(lens):
+        pg = (L + 15) // 16
+        if L % 16:
+            raw[int(bt[b, pg - 1]), L % 16:] = 0x7F
+        for j in range(pg, bt.shape[1]):
+            raw[int(bt[b, j])] = 0x7F
+    o, lse = _run(q, cache, bt, sl, rank=768, rms_offset=1000, page=16, k_scale=ks, mode="log8")
+    compare(o, lse, ref_o, ref_lse, tol=FP8_TOL, rel_tol=2e-2)
 
 def test_mtp_verify_rows(cuda_device):
     """Speculative verify: 4 draft tokens per request, flattened as the plugin's metadata builder
