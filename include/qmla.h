@@ -156,8 +156,8 @@ int qmla_mla_decode(const qmla_decode_params* p, void* stream);
  *    call on a device looks up the array's device address (cudaGetSymbolAddress) with that
  *    device current; make that first call before any stream capture.
  *  - Every call on a device shares its array, which keeps the last call's contents (the status
- *    word is cleared by each call).  Two calls whose executions overlap on the GPU (different
- *    streams, or concurrent graph replays) race on it: order them on one stream or with events.
+ *    word is cleared by each call).  Two calls whose executions overlap on the GPU (for example calls
+ *    on different streams) race on it: order them on one stream or with events.
  *  - qmla_static_read_status reads the status word of the last static call on a device. */
 int qmla_mla_decode_static(const qmla_decode_params* p, void* stream);
 
