@@ -907,6 +907,9 @@ def run_ours(args) -> None:
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
+        # the DCP merge runs over plain peer memory; NCCL carries only barriers and timing
+        # reductions here, so its NVLink SHARP (multicast) path stays off
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         # NCCL announces its version on stdout while it initialises; the driver reads exactly one
         # JSON line from stdout, so that banner goes to stderr
         sys.stdout.flush()
