@@ -658,7 +658,12 @@ int decode_impl(const qmla_decode_params* p, void* stream, bool allow_fold) {
   rc = launch_decode(p->kv_dtype == QMLA_DT_FP8E4M3, pl.cps == 2, pl.nb, pl.nqk, maps, a,
                      pl.smem_total, st);
   if (rc != QMLA_OK) return rc;
-  if (!pl.row_merge) split_merge_kernel<<<dim3(pl.work_rows, pl.R), 128, 0, st>>>(a);
+  if (!pl.row_merge) {
+    // few (row, query row) blocks: split the output dims over blocks too, so the merge has
+    // enough blocks in flight (config 4: 192 blocks -> 1152)
+    const int zsplit = (int64_t)pl.work_rows * pl.R < 1024 ? p->rank / 128 : 1;
+    split_merge_kernel<<<dim3(pl.work_rows, pl.R, zsplit), 128, 0, st>>>(a);
+  }
   return cudaGetLastError() == cudaSuccess ? QMLA_OK : QMLA_E_CUDA;
 }
 }  // namespace

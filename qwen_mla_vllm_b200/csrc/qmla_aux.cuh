@@ -83,27 +83,30 @@ __global__ void __launch_bounds__(256) bounds_kernel(const int32_t* __restrict__
 
 // Merge of the per-CTA partial segments of rows that crossed a CTA boundary
 // (the reference's stage 2, mla_decode_attention.py:1064-1137, over the
-// decode kernel's partition).  One block per (work row, query row); rows inside one CTA
-// range are final already.  Work rows of length 0 get o = 0 and lse = -inf.  Query row r
-// of work row g is head r % H of decode row g * fold + r / H.
+// decode kernel's partition).  One block per (work row, query row); with few rows the output
+// dims are also split over gridDim.z blocks of 128.  Rows inside one CTA range are final
+// already.  Work rows of length 0 get o = 0 and lse = -inf.  Query row r of work row g is head
+// r % H of decode row g * fold + r / H.  The pieces' lse values are read in parallel and each
+// thread keeps four partial loads in flight: with a serial walk over the pieces, a config-4 call
+// (8 rows cut into 18 pieces each) spent 55 us here, one dependent load at a time.
 __global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
-  const int row = blockIdx.x, r = blockIdx.y;
+  const int row = blockIdx.x, r = blockIdx.y, tid = threadIdx.x;
+  const int d0 = blockIdx.z * 128 + tid, dstep = gridDim.z * 128;  // rank is a multiple of 128
   const int plo = __ldg(a.tile_prefix + row), phi = __ldg(a.tile_prefix + row + 1);
-  const int total = __ldg(a.tile_prefix + a.num_rows);
   const int R = a.R, D = a.rank;
   const int dq = r / a.H, h = r - dq * a.H;
   const int osz = dt_size(a.o_dtype);
   uint8_t* orow = a.o + (((int64_t)row * a.fold + dq) * a.o_sr + (int64_t)h * a.o_sh) * osz;
   uint8_t* lrow = a.lse ? a.lse + (((int64_t)row * a.fold + dq) * a.lse_sr + h) * dt_size(a.lse_dtype) : nullptr;
+  const bool lse_writer = lrow && blockIdx.z == 0 && tid == 0;
   if (phi == plo) {
-    for (int d = threadIdx.x; d < D; d += blockDim.x) store_from_float(orow + d * osz, a.o_dtype, 0.f);
-    if (lrow && threadIdx.x == 0) store_from_float(lrow, a.lse_dtype, -INFINITY);
+    for (int d = d0; d < D; d += dstep) store_from_float(orow + d * osz, a.o_dtype, 0.f);
+    if (lse_writer) store_from_float(lrow, a.lse_dtype, -INFINITY);
     return;
   }
-  (void)total;
   // CTA ranges that hold tiles of this row (the decode kernel's partition, range_bounds)
   __shared__ int bnd[kMaxCtas + 1];
-  for (int c = threadIdx.x; c <= a.G; c += blockDim.x) bnd[c] = __ldg(a.range_bounds + c);
+  for (int c = tid; c <= a.G; c += blockDim.x) bnd[c] = __ldg(a.range_bounds + c);
   __syncthreads();
   auto cta_of = [&](int t) {  // the non-empty range holding tile t: largest c with bnd[c] <= t
     int lo = 0, hi = a.G;
@@ -120,9 +123,9 @@ __global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
   if (c0 == c1) return;  // the row lies inside one CTA range: already final
   __shared__ float wts[kMaxCtas];
   __shared__ int slots[kMaxCtas];
-  __shared__ float lse_g;
+  __shared__ float red[4];
   __shared__ int np_s;
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     int np = 0;  // empty ranges between c0 and c1 wrote nothing
     for (int c = c0; c <= c1; ++c)
       if (bnd[c] < bnd[c + 1]) slots[np++] = (plo <= bnd[c]) ? 2 * c : 2 * c + 1;
@@ -130,27 +133,50 @@ __global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
   }
   __syncthreads();
   const int np = np_s;
+  const int lane = tid & 31, warp = tid >> 5;
+  // m = max of the pieces' lse (log2 units), then their weights 2^(lse - m) and the sum
+  float m = -INFINITY;
+  for (int i = tid; i < np; i += blockDim.x) {
+    const float l = __ldg(a.part_lse + (int64_t)slots[i] * R + r);
+    wts[i] = l;
+    m = fmaxf(m, l);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red[warp] = m;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float m = -INFINITY;
-    for (int i = 0; i < np; ++i) m = fmaxf(m, a.part_lse[(int64_t)slots[i] * R + r]);
-    float sum = 0.f;
-    for (int i = 0; i < np; ++i) {
-      const float w = (m == -INFINITY) ? 0.f : exp2f(a.part_lse[(int64_t)slots[i] * R + r] - m);
-      wts[i] = w;
-      sum += w;
+  m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  __syncthreads();  // red[] is reused below
+  float sum = 0.f;
+  for (int i = tid; i < np; i += blockDim.x) {
+    const float w = (m == -INFINITY) ? 0.f : exp2f(wts[i] - m);
+    wts[i] = w;
+    sum += w;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (lane == 0) red[warp] = sum;
+  __syncthreads();
+  sum = (red[0] + red[1]) + (red[2] + red[3]);
+  const float inv = sum > 0.f ? 1.f / sum : 0.f;
+  // O = sum_i w_i O_i / sum: four independent partial sums, so four loads are in flight
+  const int64_t sstride = (int64_t)R * D;  // floats between consecutive slots
+  for (int d = d0; d < D; d += dstep) {
+    const float* po = a.part_o + (int64_t)r * D + d;
+    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+    int i = 0;
+    for (; i + 4 <= np; i += 4) {
+      const float v0 = __ldg(po + slots[i] * sstride), v1 = __ldg(po + slots[i + 1] * sstride);
+      const float v2 = __ldg(po + slots[i + 2] * sstride), v3 = __ldg(po + slots[i + 3] * sstride);
+      acc0 += wts[i] * v0;
+      acc1 += wts[i + 1] * v1;
+      acc2 += wts[i + 2] * v2;
+      acc3 += wts[i + 3] * v3;
     }
-    const float inv = sum > 0.f ? 1.f / sum : 0.f;
-    for (int i = 0; i < np; ++i) wts[i] *= inv;
-    lse_g = (m + log2f(sum)) * kLn2;
+    for (; i < np; ++i) acc0 += wts[i] * __ldg(po + slots[i] * sstride);
+    store_from_float(orow + d * osz, a.o_dtype, ((acc0 + acc1) + (acc2 + acc3)) * inv);
   }
-  __syncthreads();
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float acc = 0.f;
-    for (int i = 0; i < np; ++i) acc += wts[i] * a.part_o[((int64_t)slots[i] * R + r) * D + d];
-    store_from_float(orow + d * osz, a.o_dtype, acc);
-  }
-  if (lrow && threadIdx.x == 0) store_from_float(lrow, a.lse_dtype, lse_g);
+  if (lse_writer) store_from_float(lrow, a.lse_dtype, (m + log2f(sum)) * kLn2);
 }
 
 // DCP output correction for one rank (qwen_mla/dcp_fix.py:31-98): grid (B, H).
