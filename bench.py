@@ -342,10 +342,11 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(win)}
 
 
-def launches_per_call(work_rows: int) -> int:
-    """This build's kernels per qmla_mla_decode call: plan (or bounds), decode, merge."""
+def launches_per_call(work_rows: int, fp8: bool = False) -> int:
+    """This build's kernels per qmla_mla_decode call: plan (or bounds), decode, merge, and for
+    FP8 caches the Q preparation (e4m3 hi / lo rows) before the decode."""
     del work_rows
-    return 3
+    return 4 if fp8 else 3
 
 
 def capture(fns, device):
@@ -789,7 +790,7 @@ def single_gpu_line(w: Workload, device, steps: int, warmup: int, peaks: dict, g
            "algorithmic_bytes": nb, "seqs_per_s": len(w.lens) * len(list(groups)) / (ms * 1e-3),
            "roofline": {"bound": "hbm", "achieved": tbs * 1e3, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                         "frac": tbs * 1e3 / peaks["hbm_gbs"], "peak_source": peaks["kind"]},
-           "gpu_launches_per_step": launches_per_call(len(w.lens) * w.qrows) * len(params)}
+           "gpu_launches_per_step": launches_per_call(len(w.lens) * w.qrows, w.fp8) * len(params)}
     if w.qrows > 1:
         tf = fl / (ms * 1e-3) / 1e12
         res["tensor"] = {"algorithmic_flops": fl, "achieved_tflops": tf, "peak": peaks["bf16_tflops_sustained"],

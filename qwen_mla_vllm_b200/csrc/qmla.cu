@@ -183,7 +183,8 @@ struct Plan {
   int G;
   int q_vec, qpe_vec;
   // workspace offsets
-  int64_t ws_status, ws_bounds, ws_prefix, ws_done, ws_plse, ws_po, ws_total;
+  int64_t ws_status, ws_bounds, ws_prefix, ws_done, ws_plse, ws_po, ws_qimg, ws_qscale, ws_total;
+  int q_img_bytes;  // FP8: bytes of one work row's Q buffer image (0 for bf16)
   bool row_merge;  // rows cut at CTA boundaries are merged inside the decode kernel
   // smem
   uint32_t off_kring, nk, off_vring, nv, off_q, q_chunk, off_p, p_bytes, off_rms, off_misc;
@@ -377,6 +378,12 @@ int make_plan_fold(const qmla_decode_params* p, Plan* pl, int fold) {
   w = align_up(w + 4 * (int64_t)2 * G * pl->R, 256);
   pl->ws_po = w;
   w = align_up(w + 4 * (int64_t)2 * G * pl->R * p->rank, 256);
+  // FP8: every work row's Q buffer image and q scales, written by q_fp8_prep_kernel
+  pl->q_img_bytes = fp8 ? (int)q_bytes : 0;
+  pl->ws_qimg = w;
+  w = align_up(w + (int64_t)pl->q_img_bytes * pl->work_rows, 256);
+  pl->ws_qscale = w;
+  w = align_up(w + (fp8 ? 4 * (int64_t)pl->nqk * pl->work_rows : 0), 256);
   pl->ws_total = w;
   return QMLA_OK;
 }
@@ -615,6 +622,9 @@ int decode_impl(const qmla_decode_params* p, void* stream, bool allow_fold) {
   a.part_lse = reinterpret_cast<float*>(ws + pl.ws_plse);
   a.range_bounds = reinterpret_cast<const int32_t*>(ws + pl.ws_bounds);
   a.part_o = reinterpret_cast<float*>(ws + pl.ws_po);
+  a.q_img = ws + pl.ws_qimg;
+  a.q_scale = reinterpret_cast<const float*>(ws + pl.ws_qscale);
+  a.q_img_bytes = pl.q_img_bytes;
   a.row_done = pl.row_merge ? reinterpret_cast<int*>(ws + pl.ws_done) : nullptr;
   a.G = pl.G;
   a.off_kring = pl.off_kring;
@@ -655,6 +665,11 @@ int decode_impl(const qmla_decode_params* p, void* stream, bool allow_fold) {
                                      a.row_done);
   }
   if (cudaGetLastError() != cudaSuccess) return QMLA_E_CUDA;
+  if (pl.q_img_bytes > 0 && pl.work_rows > 0) {
+    q_fp8_prep_kernel<<<dim3(pl.work_rows, pl.nqk), 128, 0, st>>>(a, pl.nqk, ws + pl.ws_qimg,
+                                                                   reinterpret_cast<float*>(ws + pl.ws_qscale));
+    if (cudaGetLastError() != cudaSuccess) return QMLA_E_CUDA;
+  }
   rc = launch_decode(p->kv_dtype == QMLA_DT_FP8E4M3, pl.cps == 2, pl.nb, pl.nqk, maps, a,
                      pl.smem_total, st);
   if (rc != QMLA_OK) return rc;

@@ -179,6 +179,72 @@ __global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
   if (lse_writer) store_from_float(lrow, a.lse_dtype, (m + log2f(sum)) * kLn2);
 }
 
+// FP8 caches: each work row's Q buffer image for the decode kernel, so that the kernel stages
+// Q with plain 16-byte copies.  Query row h (head h % H of decode row g * fold + h / H) is
+// scaled by sc = 448 / max|q| to span e4m3's range and split as q * sc = hi + lo in e4m3; hi goes
+// to row h and lo to row h + nqk of the 128-byte-swizzled column chunks, exactly as the kernel
+// lays out its shared memory; rows past R and columns past qk_dim are zero.  sc goes to
+// q_scale[g * nqk + h].  One block of 128 threads per (work row, query row); a thread holds two
+// 16-element units (QK width <= 2048), all loaded before any is converted.
+__global__ void __launch_bounds__(128) q_fp8_prep_kernel(const DecodeArgs a, int nqk, uint8_t* img,
+                                                         float* q_scale) {
+  const int g = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const int R = a.R, H = a.H;
+  const int upr = a.n_sub_qk * 8;  // 16-element units per row
+  uint8_t* dst = img + (int64_t)g * a.q_img_bytes;
+  float v[2][16];
+  float mx = 0.f;
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int u = tid + 128 * k;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) v[k][e] = 0.f;
+    if (h < R && u < upr) {
+      const int dq = h / H, hh = h - dq * H;
+      const int64_t qrow = (int64_t)g * a.fold + dq;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int d = u * 16 + e;
+        if (d < a.qk_dim) {
+          const uint8_t* src = d < a.rank ? a.q + ((int64_t)qrow * a.q_sr + (int64_t)hh * a.q_sh + d) * 2
+                                          : a.q_pe + ((int64_t)qrow * a.qpe_sr + (int64_t)hh * a.qpe_sh +
+                                                      (d - a.rank)) * 2;
+          v[k][e] = load_as_float(src, a.q_dtype);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 16; ++e) mx = fmaxf(mx, fabsf(v[k][e]));
+    }
+  }
+  __shared__ float red[4];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  const float sc = mx > 0.f ? 448.f / mx : 1.f;
+  if (tid == 0 && h < R) q_scale[(int64_t)g * nqk + h] = sc;
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int u = tid + 128 * k;
+    if (u >= upr) continue;
+    uint32_t whi[4] = {0u, 0u, 0u, 0u}, wlo[4] = {0u, 0u, 0u, 0u};
+    if (h < R && u * 16 < a.qk_dim) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const float x = v[k][e] * sc;
+        const uint8_t hi = f32_to_e4m3(x);
+        const uint8_t lo = f32_to_e4m3(x - e4m3_to_f32(hi));
+        whi[e >> 2] |= (uint32_t)hi << ((e & 3) * 8);
+        wlo[e >> 2] |= (uint32_t)lo << ((e & 3) * 8);
+      }
+    }
+    uint8_t* chunk = dst + (int64_t)(u >> 3) * a.q_chunk_bytes;
+    *reinterpret_cast<uint4*>(chunk + sw128(0u, h, u & 7)) = make_uint4(whi[0], whi[1], whi[2], whi[3]);
+    *reinterpret_cast<uint4*>(chunk + sw128(0u, h + nqk, u & 7)) = make_uint4(wlo[0], wlo[1], wlo[2], wlo[3]);
+  }
+}
+
 // DCP output correction for one rank (qwen_mla/dcp_fix.py:31-98): grid (B, H).
 __global__ void dcp_correct_kernel(uint8_t* out, int out_dt, int64_t osb, int64_t osh,
                                    const float* lses, int64_t lsn, int64_t lsb, float* lse_out,

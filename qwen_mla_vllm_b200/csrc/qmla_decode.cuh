@@ -130,6 +130,9 @@ struct DecodeArgs {
   int* status;
   const int32_t* tile_prefix;   // [num_rows + 1]
   const int32_t* range_bounds;  // [G + 1] first tile of each CTA range (range_bound)
+  const uint8_t* q_img;        // FP8: per work row, the Q buffer's shared-memory image (e4m3 hi/lo)
+  const float* q_scale;        // FP8: per work row, NQK per-row q scales (448 / max|q|)
+  int q_img_bytes;             // bytes of one image (the Q buffer)
   float* part_o;               // [2*G][R][rank]
   float* part_lse;             // [2*G][R] (log2 units)
   int* row_done;               // [num_rows] pieces written per work row (in-kernel merge), or null
@@ -1167,73 +1170,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
         }
       } else {
-        // per-head scale so q*scale spans e4m3's range, then hi/lo split.  q elements
-        // come 8 at a time (one 16-byte load when the row allows it; rank is a multiple of
-        // 128, so a group of 8 never straddles the latent / rope boundary).
-        auto load8 = [&](int r, int d0, float* v) {
-          const int dq = r / H, h = r - dq * H;
-          const int64_t qrow = (int64_t)wrow * F + dq;
-          const bool lat = d0 < a.rank;
-          const uint8_t* src = lat ? a.q + ((int64_t)qrow * a.q_sr + (int64_t)h * a.q_sh + d0) * 2
-                                   : a.q_pe + ((int64_t)qrow * a.qpe_sr + (int64_t)h * a.qpe_sh +
-                                               (d0 - a.rank)) * 2;
-          if ((lat ? a.q_vec : a.qpe_vec) && d0 + 8 <= a.qk_dim && a.q_dtype == 0) {
-            const uint4 w = __ldg(reinterpret_cast<const uint4*>(src));
-            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              v[e] = __bfloat162float(__ushort_as_bfloat16((uint16_t)(ww[e >> 1] >> ((e & 1) * 16))));
-          } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              v[e] = d0 + e < a.qk_dim ? load_as_float(src + 2 * e, a.q_dtype) : 0.f;
-          }
-        };
-        for (int h = warp; h < R; h += kSoftmaxWarps) {  // h: query row
-          float mx = 0.f;
-          for (int d0 = lane * 8; d0 < a.qk_dim; d0 += 256) {
-            float v[8];
-            load8(h, d0, v);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(v[e]));
-          }
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-          if (lane == 0) hv[192 + h] = mx > 0.f ? 448.f / mx : 1.f;
-        }
-        named_bar_sync(kBarSoftmax, kSoftmaxThreads);
-        // one 16-element unit of one head per step: its hi bytes go to row h, lo to h + nqk
-        const int upr = a.n_sub_qk * 8;  // 16-byte units (16 e4m3) per Q row
-        for (int i = tid; i < nqk * upr; i += kSoftmaxThreads) {
-          const int h = i / upr, u = i - h * upr, d0 = u * 16;
-          uint32_t whi[4] = {0u, 0u, 0u, 0u}, wlo[4] = {0u, 0u, 0u, 0u};
-          if (h < R && d0 < a.qk_dim) {
-            const float sc = hv[192 + h];
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {  // 8 elements at a time
-              float v[8];
-              if (d0 + 8 * half < a.qk_dim) {
-                load8(h, d0 + 8 * half, v);
-              } else {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) v[e] = 0.f;
-              }
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const float x = v[e] * sc;
-                const uint8_t hi = f32_to_e4m3(x);
-                const uint8_t lo = f32_to_e4m3(x - e4m3_to_f32(hi));
-                const int k = 8 * half + e;
-                whi[k >> 2] |= (uint32_t)hi << ((k & 3) * 8);
-                wlo[k >> 2] |= (uint32_t)lo << ((k & 3) * 8);
-              }
-            }
-          }
-          st_shared_v4(sw128(qbuf + (u >> 3) * a.q_chunk_bytes, h, u & 7), whi[0], whi[1], whi[2],
-                       whi[3]);
-          st_shared_v4(sw128(qbuf + (u >> 3) * a.q_chunk_bytes, h + nqk, u & 7), wlo[0], wlo[1],
-                       wlo[2], wlo[3]);
-        }
+        // The e4m3 hi / lo rows and the per-row scales were prepared for every work row by
+        // q_fp8_prep_kernel (the image of this buffer): one 16-byte cp.async per unit, all in
+        // flight at once.  (Converting here took one round trip to memory per unit of a thread:
+        // ~30 us per row segment at 24 query rows, ~80 us at 48.)
+        const uint8_t* img = a.q_img + (int64_t)wrow * a.q_img_bytes;
+        for (int i = tid; i < (a.q_img_bytes >> 4); i += kSoftmaxThreads) cp_async_16(qbuf + 16 * i, img + 16 * i, 16u);
+        if (tid < R) hv[192 + tid] = __ldg(a.q_scale + (int64_t)wrow * NQK + tid);
+        asm volatile("cp.async.wait_all;" ::: "memory");
       }
       fence_proxy_async_smem();
       named_bar_sync(kBarSoftmax, kSoftmaxThreads);
