@@ -600,6 +600,8 @@ int decode_impl(const qmla_decode_params* p, void* stream, bool allow_fold) {
   // a row segment's fixed overhead, in tiles, for the work partition (test hook QMLA_SEG_COST)
   a.seg_cost = 2;  // swept 0-4: 2 best on a DCP rank's shard (+17% over 0), config 1 and GLA flat
   if (const char* e = getenv("QMLA_SEG_COST")) a.seg_cost = std::max(0, std::min(atoi(e), 64));
+  a.early_q = kEarlyQTiles;  // test hook QMLA_EARLY_Q: the longest segment that stages Q early
+  if (const char* e = getenv("QMLA_EARLY_Q")) a.early_q = std::max(0, atoi(e));
 
   a.rms_base_b = pl.rms_base_b;
   a.rms_units = pl.rms_units;

@@ -112,6 +112,7 @@ struct DecodeArgs {
   int n_sub_qk;     // 128-byte-wide MMA sub-chunks of the QK width
   int n_full_chunks;  // chunks that lie entirely inside the QK width
   int seg_cost;       // work-partition cost of a row's segment overhead, in tiles
+  int early_q;        // segments of at most this many tiles stage the next segment's Q early
   int rms_base_b;   // 16-byte-aligned first byte of the rms tail in a row
   int rms_units;    // 16-byte units staged per token (0: no rms); staging stride = 16 * rms_units
   int rms_skip;     // first rms byte within the staged units
@@ -1464,7 +1465,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       // complete): the next QK then overlaps this segment's PV tail and epilogue.  After a
       // long segment the boundary costs little, and staging Q while the V loads stream
       // measured 2% slower on config 1, so Q is staged after the epilogue there.
-      const bool early = k1 - k0 <= kEarlyQTiles;
+      const bool early = k1 - k0 <= a.early_q;
       if (early) {
         const int nrow = peek_segment_row(a.tile_prefix, cur);
         if (nrow >= 0) stage_q(nrow);
